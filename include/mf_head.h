@@ -1,0 +1,177 @@
+/*
+ * mf_head.h — C-ABI of the B200 DFA-restricted output head.
+ *
+ * Every entry point takes plain device pointers with their sizes in bytes,
+ * a cudaStream_t passed as `void*`, and returns an mf_status whose `code`
+ * uses the numbering of the reference's marketforge::ErrorCode
+ * (include/marketforge/core/status.hpp:7-31), so a C++ wrapper converts it
+ * to marketforge::Status by a cast.  All launches are asynchronous on the
+ * given stream; arguments are validated on the host before any launch, in
+ * the reference's order (src/cuda/greedy.cu:349-399):
+ *   zero dims / zero maximum / null stream        -> MF_INVALID_ARGUMENT
+ *   vocab or maximum > UINT32_MAX, rows > INT_MAX -> MF_RESOURCE_LIMIT
+ *   a size product overflowing uint64             -> MF_ARITHMETIC_OVERFLOW
+ *   a byte size that does not match exactly, a null or aliased buffer
+ *                                                 -> MF_INVALID_ARGUMENT
+ *   the launch failing                            -> MF_CUDA_BACKEND_FAILURE,
+ *                                                    detail = cudaError_t
+ * Bad rows found on the device produce MF_INVALID_TOKEN, never a trap.
+ *
+ * Selection rule shared by every head/select entry point: the highest FP32
+ * score wins, equal scores resolve to the lowest token id, NaN never wins,
+ * and a valid row whose every score is NaN selects its lowest candidate id.
+ */
+#ifndef MF_HEAD_H
+#define MF_HEAD_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MF_API __attribute__((visibility("default")))
+#else
+#define MF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* marketforge::ErrorCode values used here (status.hpp:7-31). */
+enum {
+  MF_OK = 0,
+  MF_INVALID_ARGUMENT = 1,
+  MF_ARITHMETIC_OVERFLOW = 5,
+  MF_RESOURCE_LIMIT = 15,
+  MF_CUDA_BACKEND_FAILURE = 21,
+  MF_CUDA_RUNTIME_FAILURE = 22
+};
+
+/* marketforge::Status (status.hpp:33-49) as a C struct. */
+typedef struct mf_status {
+  int32_t code;
+  uint32_t detail;
+} mf_status;
+
+/* restricted_greedy_invalid_token_id (include/marketforge/cuda/greedy.hpp:11-12). */
+#define MF_INVALID_TOKEN 0xFFFFFFFFu
+
+/* Library version and the device architecture it was built for (1000 = sm_100a). */
+MF_API uint32_t mf_version(void);
+MF_API uint32_t mf_built_arch(void);
+
+/* ---- reference-signature entry points ----------------------------------- */
+
+/* Replaces marketforge::cuda::greedy_select_f16
+ * (include/marketforge/cuda/greedy.hpp:17-21, src/cuda/greedy.cu:237-279).
+ * logits: fp16 [rows, vocab]; token_ids: u32 [rows].  All-NaN rows select 0. */
+MF_API mf_status mf_greedy_select_f16(const void* logits, uint64_t logits_bytes,
+                               void* token_ids, uint64_t token_ids_bytes,
+                               uint64_t rows, uint64_t vocab, void* stream);
+
+/* Replaces marketforge::cuda::restricted_greedy_select_f16
+ * (greedy.hpp:29-33, greedy.cu:281-347).  allowed: u32 [rows, max_allowed],
+ * counts: u32 [rows].  count 0, count > max_allowed or a candidate >= vocab
+ * gives MF_INVALID_TOKEN for that row. */
+MF_API mf_status mf_restricted_greedy_select_f16(const void* logits, uint64_t logits_bytes,
+                                          const void* allowed, uint64_t allowed_bytes,
+                                          const void* counts, uint64_t counts_bytes,
+                                          void* token_ids, uint64_t token_ids_bytes,
+                                          uint64_t rows, uint64_t vocab,
+                                          uint64_t max_allowed, void* stream);
+
+/* Replaces marketforge::cuda::restricted_output_head_f16
+ * (greedy.hpp:43-49, greedy.cu:349-414): the fused gather-GEMV + argmax over
+ * a padded candidate table.  hidden: fp16 [rows, hidden_size]; embedding:
+ * fp16 [vocab, hidden_size]; allowed: u32 [rows, max_allowed]; counts: u32
+ * [rows]; token_ids: u32 [rows].  Needs no workspace: each row is owned by
+ * one thread block. */
+MF_API mf_status mf_restricted_output_head_f16(const void* hidden, uint64_t hidden_bytes,
+                                        const void* embedding, uint64_t embedding_bytes,
+                                        const void* allowed, uint64_t allowed_bytes,
+                                        const void* counts, uint64_t counts_bytes,
+                                        void* token_ids, uint64_t token_ids_bytes,
+                                        uint64_t rows, uint64_t hidden_size,
+                                        uint64_t vocab, uint64_t max_allowed,
+                                        void* stream);
+
+/* ---- ragged CSR head (new batched launch path) --------------------------
+ *
+ * Row r's candidates are ids[offsets[r] .. offsets[r+1]) (i32), the flat
+ * form the callers built as a padded table from TokenDfa::allowed
+ * (src/tools/cuda_restricted_greedy_bench.cu:107-165).  The candidates of
+ * the whole batch are split evenly over the GPU, so one long row is shared
+ * by many thread blocks; partial results merge through 64-bit atomic max on
+ * a packed (score, id) key in `workspace`, which makes the result
+ * independent of scheduling.
+ *
+ * workspace: mf_head_workspace_bytes(rows) bytes of device memory, zero-filled
+ * once by the caller before its first use; every call leaves it zero again.
+ * Calls that share a workspace must not overlap on the GPU.
+ * out_ids: u32 [rows]; out_scores: f32 [rows] or NULL (the winning FP32 score,
+ * NaN for all-NaN or invalid rows).  Empty rows and rows with a candidate
+ * outside [0, vocab) give MF_INVALID_TOKEN.  If the offsets are malformed
+ * (offsets[0] != 0, decreasing, or offsets[rows] != total_ids) every row gives
+ * MF_INVALID_TOKEN; the kernel never reads outside ids[0, total_ids). */
+MF_API uint64_t mf_head_workspace_bytes(uint64_t rows);
+
+MF_API mf_status mf_head_restricted_csr_f16(const void* hidden, uint64_t hidden_bytes,
+                                     const void* embedding, uint64_t embedding_bytes,
+                                     const void* offsets, uint64_t offsets_bytes,
+                                     const void* ids, uint64_t ids_bytes,
+                                     void* out_ids, uint64_t out_ids_bytes,
+                                     void* out_scores, uint64_t out_scores_bytes,
+                                     void* workspace, uint64_t workspace_bytes,
+                                     uint64_t rows, uint64_t hidden_size,
+                                     uint64_t vocab, void* stream);
+
+/* ---- device-resident DFA: allowed-set lookup + head + advance ------------
+ *
+ * The DFA is CSR over states, the flat form of TokenDfa/ActionDfa's
+ * StateRecord{first_arc, arc_count} + GrammarArc{token, next}
+ * (include/marketforge/grammar/token_dfa.hpp:54-58, action_dfa.hpp:20-27):
+ * state s allows tokens arc_tokens[state_offsets[s] .. state_offsets[s+1])
+ * (sorted ascending, as TokenDfa::build emits them) and taking the k-th arc
+ * moves to arc_next[k].  One step: for each sequence b, look up the allowed
+ * set of states_in[b], run the restricted head on hidden[b], write the
+ * chosen token to out_tokens[b] and the next state to states_out[b]
+ * (TokenDfa::advance, src/grammar/token_dfa.cpp:111-128).  A sequence whose
+ * state is out of range or has no arcs gets MF_INVALID_TOKEN and keeps its
+ * state.  The workspace rule is the same as for the CSR head, sized by
+ * mf_dfa_workspace_bytes(batch). */
+MF_API uint64_t mf_dfa_workspace_bytes(uint64_t batch);
+
+MF_API mf_status mf_dfa_head_step_f16(const void* hidden, uint64_t hidden_bytes,
+                               const void* embedding, uint64_t embedding_bytes,
+                               const void* state_offsets, uint64_t state_offsets_bytes,
+                               const void* arc_tokens, uint64_t arc_tokens_bytes,
+                               const void* arc_next, uint64_t arc_next_bytes,
+                               const void* states_in, uint64_t states_in_bytes,
+                               void* states_out, uint64_t states_out_bytes,
+                               void* out_tokens, uint64_t out_tokens_bytes,
+                               void* out_scores, uint64_t out_scores_bytes,
+                               void* workspace, uint64_t workspace_bytes,
+                               uint64_t batch, uint64_t num_states, uint64_t hidden_size,
+                               uint64_t vocab, void* stream);
+
+/* `steps` DFA head steps back to back on one stream with no host
+ * synchronisation: hidden is fp16 [steps, batch, hidden_size];
+ * state_trace is u32 [steps + 1, batch] with row 0 holding the initial
+ * states; token_trace is u32 [steps, batch]; score_trace f32 [steps, batch]
+ * or NULL.  Step s reads state_trace[s] and writes state_trace[s + 1]. */
+MF_API mf_status mf_dfa_decode_f16(const void* hidden, uint64_t hidden_bytes,
+                            const void* embedding, uint64_t embedding_bytes,
+                            const void* state_offsets, uint64_t state_offsets_bytes,
+                            const void* arc_tokens, uint64_t arc_tokens_bytes,
+                            const void* arc_next, uint64_t arc_next_bytes,
+                            void* state_trace, uint64_t state_trace_bytes,
+                            void* token_trace, uint64_t token_trace_bytes,
+                            void* score_trace, uint64_t score_trace_bytes,
+                            void* workspace, uint64_t workspace_bytes,
+                            uint64_t steps, uint64_t batch, uint64_t num_states,
+                            uint64_t hidden_size, uint64_t vocab, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MF_HEAD_H */

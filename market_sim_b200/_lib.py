@@ -1,0 +1,75 @@
+"""ctypes binding of ``libmfhead.so`` (the C-ABI in ``include/mf_head.h``).
+
+The library is the product: there is no Python or CPU fallback.  Importing
+this module fails loudly when the shared library is missing; build it with
+``python -m market_sim_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libmfhead.so")
+
+
+class MfStatus(ctypes.Structure):
+    """``mf_status``: ``code`` uses marketforge::ErrorCode numbering."""
+
+    _fields_ = [("code", ctypes.c_int32), ("detail", ctypes.c_uint32)]
+
+
+_P = ctypes.c_void_p
+_U64 = ctypes.c_uint64
+
+# name -> argument count of (pointer, bytes) pairs and trailing u64 / stream args
+_SIGNATURES = {
+    "mf_greedy_select_f16": [_P, _U64, _P, _U64, _U64, _U64, _P],
+    "mf_restricted_greedy_select_f16": [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _U64, _U64, _U64, _P],
+    "mf_restricted_output_head_f16": [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
+                                      _U64, _U64, _U64, _U64, _P],
+    "mf_head_restricted_csr_f16": [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
+                                   _P, _U64, _U64, _U64, _U64, _P],
+    "mf_dfa_head_step_f16": [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
+                             _P, _U64, _P, _U64, _P, _U64, _U64, _U64, _U64, _U64, _P],
+    "mf_dfa_decode_f16": [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
+                          _P, _U64, _P, _U64, _U64, _U64, _U64, _U64, _U64, _P],
+}
+
+_U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64]}
+_U32_FUNCS = {"mf_version": [], "mf_built_arch": []}
+
+# Optional entry points: bound when the library exports them.
+_OPTIONAL: dict[str, list] = {}
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library with "
+            "`python -m market_sim_b200.build` (no CPU fallback exists)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, args in _SIGNATURES.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = MfStatus
+    for name, args in _U64_FUNCS.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = ctypes.c_uint64
+    for name, args in _U32_FUNCS.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = ctypes.c_uint32
+    for name, args in _OPTIONAL.items():
+        f = getattr(lib, name, None)
+        if f is not None:
+            f.argtypes = args
+            f.restype = MfStatus
+    return lib
+
+
+lib = _load()
+
+#: every symbol include/mf_head.h declares (checked by the CPU test suite)
+EXPORTED = sorted(list(_SIGNATURES) + list(_U64_FUNCS) + list(_U32_FUNCS))

@@ -1,0 +1,619 @@
+// Ragged (CSR) restricted output head and the device-resident DFA step.
+//
+// Reference behaviour: restricted_output_head_kernel, src/cuda/greedy.cu:133-212
+// (one thread block per row, one thread per candidate walking the 576-wide
+// row 2 bytes at a time).  Here the candidates of the whole batch are laid
+// out flat (CSR) and split evenly over every 8-lane group on the GPU, so a
+// 4096-candidate row is shared by hundreds of groups while a 1-candidate row
+// costs one group-iteration:
+//
+//   * a group of 8 lanes reads one embedding row per iteration as 9 x 16 B
+//     coalesced loads per lane (1152 B per row), two rows in flight;
+//   * the hidden row sits in registers as fp16 (36 x u32 per lane) and the
+//     dot product uses sm_100's f16 x f16 -> f32 FMA, then a 3-step shuffle;
+//   * each group keeps a running packed (score, id) key per row; a row owned
+//     by one group is finalised straight from registers, a row shared by
+//     several groups merges with atomicMax on a 64-bit key in the workspace
+//     and the group that completes the row's candidate count finalises it
+//     (per-row arrival counter).  Max is order-independent, so results are
+//     deterministic.
+//
+// Workspace layout (zero between calls; every call returns it to zero):
+//   keys  u64[rows] | count u32[rows] | control u32[4] (done, anomaly, -, -)
+#include <cuda_runtime.h>
+
+#include <initializer_list>
+
+#include "common.cuh"
+
+namespace mfb {
+
+enum class RowMode { kCsr, kDfa };
+
+struct RaggedParams {
+  const __half* hidden;
+  const __half* embedding;
+  // CSR mode: offsets[rows+1] and ids[total].
+  const int32_t* offsets;
+  const int32_t* ids;
+  int64_t total;
+  // DFA mode: states_in[rows] index state_offsets[num_states+1] into
+  // arc_tokens / arc_next[num_arcs].
+  const int32_t* state_offsets;
+  const uint32_t* arc_next;
+  const uint32_t* states_in;
+  uint32_t* states_out;
+  uint32_t num_states;
+  int64_t num_arcs;
+  // outputs
+  uint32_t* out_ids;
+  float* out_scores;
+  // workspace
+  unsigned long long* keys;
+  uint32_t* counts;
+  uint32_t* control;
+  uint32_t rows;
+  uint32_t hidden_size;
+  uint32_t vocab;
+};
+
+constexpr int kThreads = 256;
+constexpr int kGroupsPerBlock = kThreads / 8;
+constexpr int kMaxDfaBatch = 8192;
+
+// Row-start table for one row mode.  CSR reads global offsets; DFA mode
+// builds the prefix sum of the allowed-set sizes in shared memory.
+template <RowMode M>
+struct Rows;
+
+template <>
+struct Rows<RowMode::kCsr> {
+  const int32_t* start;  // global, rows + 1 entries
+  __device__ __forceinline__ int64_t at(uint32_t r) const { return start[r]; }
+};
+
+template <>
+struct Rows<RowMode::kDfa> {
+  const int32_t* start;  // shared, rows + 1 entries
+  __device__ __forceinline__ int64_t at(uint32_t r) const { return start[r]; }
+};
+
+// Largest r in [0, rows) with at(r) <= c (rows assumed non-decreasing);
+// 8-ary search shared by the 8 lanes of a group.
+template <RowMode M>
+__device__ uint32_t find_row(const Rows<M>& rows_tab, uint32_t rows, int64_t c, int sub,
+                             unsigned gmask) {
+  uint32_t lo = 0, hi = rows;  // answer in [lo, hi)
+  while (hi - lo > 1) {
+    const uint32_t span = hi - lo;
+    const uint32_t step = (span + 7) / 8;
+    const uint32_t probe = lo + (uint32_t)sub * step;
+    const bool ok = probe < hi && rows_tab.at(probe) <= c;
+    const unsigned ballot = __ballot_sync(gmask, ok) & gmask;
+    // lanes are ordered by probe; the last lane with ok gives the new lo
+    const int last = 31 - __clz(ballot);
+    const int lane_base = (threadIdx.x & 31) & ~7;
+    const uint32_t new_lo = lo + (uint32_t)(last >= 0 ? last - lane_base : 0) * step;
+    const uint32_t new_hi = min(hi, new_lo + step);
+    lo = new_lo;
+    hi = new_hi;
+  }
+  return lo;
+}
+
+// Writes the final result of row r from its merged key.
+template <RowMode M>
+__device__ void finalize_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32_t r,
+                             unsigned long long key) {
+  if (M == RowMode::kCsr) {
+    const bool ok = key_is_result(key);
+    p.out_ids[r] = ok ? key_id(key) : kInvalid;
+    if (p.out_scores) p.out_scores[r] = ok ? key_score(key) : __uint_as_float(0x7FC00000u);
+  } else {
+    const uint32_t st = p.states_in[r];
+    if (key_is_result(key)) {
+      const int64_t arc = (int64_t)p.state_offsets[st] + key_id(key);
+      p.out_ids[r] = (uint32_t)p.ids[arc];
+      p.states_out[r] = p.arc_next[arc];
+      if (p.out_scores) p.out_scores[r] = key_score(key);
+    } else {
+      p.out_ids[r] = kInvalid;
+      p.states_out[r] = st;
+      if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+    }
+  }
+}
+
+// Load the hidden row r's 9 chunks owned by this lane (fast path).
+__device__ __forceinline__ void load_hidden_fast(const __half* hidden, uint32_t r, int sub,
+                                                 uint4 (&h)[kFastChunksPerLane]) {
+  const uint4* row = reinterpret_cast<const uint4*>(hidden + (size_t)r * kFastHidden);
+#pragma unroll
+  for (int k = 0; k < kFastChunksPerLane; ++k) h[k] = ld_v4(row + sub + 8 * k);
+}
+
+// Dot product of hidden row r with embedding row t by one 8-lane group:
+// generic path for any width (used by the small known-answer shapes).
+__device__ float group_dot_generic(const __half* hidden, const __half* emb, uint32_t r,
+                                   uint32_t t, uint32_t width, int sub, unsigned gmask) {
+  float a = 0.f;
+  const __half* h = hidden + (size_t)r * width;
+  const __half* e = emb + (size_t)t * width;
+  for (uint32_t f = sub; f < width; f += 8) a = fmaf(__half2float(h[f]), __half2float(e[f]), a);
+  return group8_sum(a, gmask);
+}
+
+// One flushed (row, key, n) triple: merge and finalise when complete.
+template <RowMode M>
+__device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32_t r,
+                          int64_t row_len, unsigned long long key, int64_t n, int sub) {
+  if (sub != 0 || n <= 0) return;
+  if (n == row_len) {  // the group saw the whole row: no merge needed
+    finalize_row<M>(p, rows_tab, r, key);
+    return;
+  }
+  if (key != kKeyNone) atomicMax(p.keys + r, key);
+  __threadfence();
+  const uint32_t before = atomicAdd(p.counts + r, (uint32_t)n);
+  if ((int64_t)before + n == row_len) {
+    __threadfence();
+    const unsigned long long merged = atomicExch(p.keys + r, 0ull);
+    p.counts[r] = 0u;
+    finalize_row<M>(p, rows_tab, r, merged);
+  }
+}
+
+template <RowMode M, bool kFast>
+__global__ void __launch_bounds__(kThreads, 2)
+ragged_head_kernel(RaggedParams p, int64_t chunk) {
+  extern __shared__ int32_t smem_rows[];  // DFA mode: rows + 1 starts
+  __shared__ uint32_t s_last;
+
+  Rows<M> rows_tab;
+  int64_t total;
+  if (M == RowMode::kCsr) {
+    rows_tab.start = p.offsets;
+    total = p.total;
+    // Prologue: empty rows get the sentinel here (no group visits them);
+    // decreasing offsets or a bad first/last offset flag the batch.
+    for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows;
+         r += gridDim.x * kThreads) {
+      const int32_t b = p.offsets[r], e = p.offsets[r + 1];
+      if (e < b) {
+        atomicOr(p.control + 1, 1u);
+      } else if (e == b) {
+        p.out_ids[r] = kInvalid;
+        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+      }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0 &&
+        (p.offsets[0] != 0 || (int64_t)p.offsets[p.rows] != p.total))
+      atomicOr(p.control + 1, 1u);
+  } else {
+    // Allowed-set lookup: per-sequence candidate counts from the DFA, and
+    // their exclusive prefix sum in shared memory (every block computes the
+    // same table).  Invalid states and empty sets get the sentinel.
+    const uint32_t rows = p.rows;
+    for (uint32_t r = threadIdx.x; r < rows; r += kThreads) {
+      const uint32_t st = p.states_in[r];
+      int32_t len = 0;
+      if (st < p.num_states) {
+        const int32_t b = p.state_offsets[st], e = p.state_offsets[st + 1];
+        if (b >= 0 && e > b && (int64_t)e <= p.num_arcs) len = e - b;
+      }
+      smem_rows[r + 1] = len;
+      if (len == 0 && (r % gridDim.x) == blockIdx.x) {
+        p.out_ids[r] = kInvalid;
+        p.states_out[r] = st;
+        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+      }
+    }
+    if (threadIdx.x == 0) smem_rows[0] = 0;
+    __syncthreads();
+    // inclusive scan of smem_rows[1..rows] (serial per warp chunk is fine
+    // for <= 8192 rows: one warp scans, 32 lanes x chunks)
+    if (threadIdx.x < 32) {
+      const uint32_t per = (rows + 31) / 32;
+      const uint32_t b = 1 + threadIdx.x * per;
+      const uint32_t e = min(rows + 1, b + per);
+      int32_t run = 0;
+      for (uint32_t i = b; i < e; ++i) run += smem_rows[i];
+      int32_t incl = run;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if ((int)threadIdx.x >= o) incl += v;
+      }
+      int32_t acc = incl - run;
+      for (uint32_t i = b; i < e; ++i) {
+        acc += smem_rows[i];
+        smem_rows[i] = acc;
+      }
+    }
+    __syncthreads();
+    rows_tab.start = smem_rows;
+    total = smem_rows[rows];
+    const int64_t groups = (int64_t)gridDim.x * kGroupsPerBlock;
+    chunk = (total + groups - 1) / groups;
+    if (chunk < 4) chunk = 4;
+  }
+
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 7;
+  const unsigned gmask = 0xFFu << (lane & ~7);
+  const int64_t group = (int64_t)blockIdx.x * kGroupsPerBlock + (threadIdx.x >> 3);
+  const int64_t c_begin = group * chunk;
+  const int64_t c_end = min(total, c_begin + chunk);
+
+  if (c_begin < c_end) {
+    uint32_t r = find_row<M>(rows_tab, p.rows, c_begin, sub, gmask);
+    int64_t row_b = rows_tab.at(r);
+    int64_t row_e = rows_tab.at(r + 1);
+    const int32_t* cand;  // candidate token ids of the current row, by flat index
+    cand = (M == RowMode::kCsr) ? p.ids : nullptr;
+    int64_t arc_base = 0;  // DFA: flat index -> arc index offset
+    if (M == RowMode::kDfa) arc_base = (int64_t)p.state_offsets[p.states_in[r]] - row_b;
+
+    uint4 h[kFastChunksPerLane];
+    if (kFast) load_hidden_fast(p.hidden, r, sub, h);
+    unsigned long long best = kKeyNone;
+    int64_t seen = 0;
+
+    for (int64_t c = c_begin; c < c_end;) {
+      // advance to the row that holds c (rows with no candidates are skipped)
+      if (c >= row_e) {
+        flush_row<M>(p, rows_tab, r, row_e - row_b, best, seen, sub);
+        best = kKeyNone;
+        seen = 0;
+        while (c >= row_e && r + 1 < p.rows) {
+          ++r;
+          row_b = row_e;
+          row_e = rows_tab.at(r + 1);
+        }
+        if (c >= row_e || c < row_b) break;  // malformed offsets: stop
+        if (M == RowMode::kDfa) arc_base = (int64_t)p.state_offsets[p.states_in[r]] - row_b;
+        if (kFast) load_hidden_fast(p.hidden, r, sub, h);
+      }
+      // up to two candidates of this row per iteration
+      const int64_t n_here = min(min(c_end, row_e) - c, (int64_t)2);
+      uint32_t t0, t1 = 0;
+      if (M == RowMode::kCsr) {
+        t0 = (uint32_t)cand[c];
+        if (n_here > 1) t1 = (uint32_t)cand[c + 1];
+      } else {
+        t0 = (uint32_t)p.ids[arc_base + c];
+        if (n_here > 1) t1 = (uint32_t)p.ids[arc_base + c + 1];
+      }
+      const bool v0 = t0 < p.vocab;
+      const bool v1 = n_here > 1 && t1 < p.vocab;
+      const uint32_t id0 = (M == RowMode::kCsr) ? t0 : (uint32_t)(c - row_b);
+      const uint32_t id1 = (M == RowMode::kCsr) ? t1 : (uint32_t)(c + 1 - row_b);
+      float s0, s1 = 0.f;
+      if (kFast) {
+        uint4 e0[kFastChunksPerLane], e1[kFastChunksPerLane];
+        const uint4* row0 = reinterpret_cast<const uint4*>(p.embedding + (size_t)(v0 ? t0 : 0) * kFastHidden);
+        const uint4* row1 = reinterpret_cast<const uint4*>(p.embedding + (size_t)(v1 ? t1 : 0) * kFastHidden);
+        if (v0) {
+#pragma unroll
+          for (int k = 0; k < kFastChunksPerLane; ++k) e0[k] = ld_stream_v4(row0 + sub + 8 * k);
+        }
+        if (v1) {
+#pragma unroll
+          for (int k = 0; k < kFastChunksPerLane; ++k) e1[k] = ld_stream_v4(row1 + sub + 8 * k);
+        }
+        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+        if (v0) {
+#pragma unroll
+          for (int k = 0; k < kFastChunksPerLane; ++k) dot_v4(a0, a1, h[k], e0[k]);
+        }
+        if (v1) {
+#pragma unroll
+          for (int k = 0; k < kFastChunksPerLane; ++k) dot_v4(b0, b1, h[k], e1[k]);
+        }
+        s0 = group8_sum(a0 + a1, gmask);
+        s1 = group8_sum(b0 + b1, gmask);
+      } else {
+        s0 = v0 ? group_dot_generic(p.hidden, p.embedding, r, t0, p.hidden_size, sub, gmask) : 0.f;
+        if (n_here > 1)
+          s1 = v1 ? group_dot_generic(p.hidden, p.embedding, r, t1, p.hidden_size, sub, gmask) : 0.f;
+      }
+      best = umax64(best, v0 ? make_key(s0, id0) : kKeyPoison);
+      if (n_here > 1) best = umax64(best, v1 ? make_key(s1, id1) : kKeyPoison);
+      seen += n_here;
+      c += n_here;
+    }
+    flush_row<M>(p, rows_tab, r, row_e - row_b, best, seen, sub);
+  }
+
+  // Last block out: if the batch was flagged malformed, give every row the
+  // sentinel and clear the whole workspace; then reset the control words.
+  // Every thread fences first so its atomics and result stores are ordered
+  // before this block's arrival on the done counter.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = (atomicAdd(p.control, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    const uint32_t anomaly = atomicAdd(p.control + 1, 0u);
+    if (anomaly) {
+      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+        p.keys[r] = 0ull;
+        p.counts[r] = 0u;
+        p.out_ids[r] = kInvalid;
+        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      p.control[1] = 0u;
+      p.control[0] = 0u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+struct DeviceInfo {
+  int sms = 0;
+  int blocks_per_sm[2][2] = {{0, 0}, {0, 0}};  // [mode][fast]
+};
+
+static DeviceInfo& device_info() {
+  static DeviceInfo info[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo& d = info[dev & 63];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &d.blocks_per_sm[0][0], ragged_head_kernel<RowMode::kCsr, false>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &d.blocks_per_sm[0][1], ragged_head_kernel<RowMode::kCsr, true>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &d.blocks_per_sm[1][0], ragged_head_kernel<RowMode::kDfa, false>, kThreads, 4096);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &d.blocks_per_sm[1][1], ragged_head_kernel<RowMode::kDfa, true>, kThreads, 4096);
+    for (auto& m : d.blocks_per_sm)
+      for (int& b : m)
+        if (b < 1) b = 1;
+  }
+  return d;
+}
+
+}  // namespace mfb
+
+using namespace mfb;
+
+namespace {
+
+mf_status ok() { return mf_status{MF_OK, 0}; }
+mf_status fail(int32_t code, uint32_t detail = 0) { return mf_status{code, detail}; }
+
+bool mul_ok(uint64_t a, uint64_t b, uint64_t* out) {
+  if (a != 0 && b > UINT64_MAX / a) return false;
+  *out = a * b;
+  return true;
+}
+
+bool distinct(std::initializer_list<const void*> ptrs) {
+  const void* seen[16];
+  int n = 0;
+  for (const void* p : ptrs) {
+    if (p == nullptr) return false;
+    for (int i = 0; i < n; ++i)
+      if (seen[i] == p) return false;
+    seen[n++] = p;
+  }
+  return true;
+}
+
+bool fast_path(const void* hidden, const void* embedding, uint64_t hidden_size) {
+  return hidden_size == (uint64_t)kFastHidden && ((uintptr_t)hidden % 16) == 0 &&
+         ((uintptr_t)embedding % 16) == 0;
+}
+
+mf_status launch_status(cudaError_t e) {
+  return e == cudaSuccess ? ok() : fail(MF_CUDA_BACKEND_FAILURE, (uint32_t)e);
+}
+
+}  // namespace
+
+extern "C" uint64_t mf_head_workspace_bytes(uint64_t rows) {
+  // keys u64[rows] + counts u32[rows] + control u32[4], 16-byte multiple
+  const uint64_t b = rows * 12 + 16;
+  return (b + 15) & ~15ull;
+}
+
+extern "C" uint64_t mf_dfa_workspace_bytes(uint64_t batch) { return mf_head_workspace_bytes(batch); }
+
+namespace {
+
+void split_workspace(void* ws, uint64_t rows, RaggedParams& p) {
+  char* b = static_cast<char*>(ws);
+  p.keys = reinterpret_cast<unsigned long long*>(b);
+  p.counts = reinterpret_cast<uint32_t*>(b + rows * 8);
+  p.control = reinterpret_cast<uint32_t*>(b + rows * 12);
+}
+
+}  // namespace
+
+extern "C" mf_status mf_head_restricted_csr_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
+    uint64_t vocab, void* stream) {
+  if (rows == 0 || hidden_size == 0 || vocab == 0 || stream == nullptr)
+    return fail(MF_INVALID_ARGUMENT);
+  if (vocab > UINT32_MAX || hidden_size > UINT32_MAX || rows > (uint64_t)INT32_MAX - 1)
+    return fail(MF_RESOURCE_LIMIT);
+  uint64_t hb, eb, ob;
+  if (!mul_ok(rows, hidden_size, &hb) || !mul_ok(hb, 2, &hb) ||
+      !mul_ok(vocab, hidden_size, &eb) || !mul_ok(eb, 2, &eb) || !mul_ok(rows + 1, 4, &ob))
+    return fail(MF_ARITHMETIC_OVERFLOW);
+  if (ids_bytes % 4 != 0 || ids_bytes / 4 > (uint64_t)INT32_MAX) return fail(MF_INVALID_ARGUMENT);
+  if (hidden_bytes != hb || embedding_bytes != eb || offsets_bytes != ob ||
+      out_ids_bytes != rows * 4 || (out_scores && out_scores_bytes != rows * 4) ||
+      workspace_bytes < mf_head_workspace_bytes(rows))
+    return fail(MF_INVALID_ARGUMENT);
+  if (!distinct({hidden, embedding, offsets, out_ids, workspace}) ||
+      (ids_bytes && !distinct({ids, hidden, embedding, offsets, out_ids, workspace})) ||
+      (out_scores && !distinct({out_scores, hidden, embedding, offsets, out_ids, workspace})))
+    return fail(MF_INVALID_ARGUMENT);
+
+  RaggedParams p{};
+  p.hidden = static_cast<const __half*>(hidden);
+  p.embedding = static_cast<const __half*>(embedding);
+  p.offsets = static_cast<const int32_t*>(offsets);
+  p.ids = static_cast<const int32_t*>(ids);
+  p.total = (int64_t)(ids_bytes / 4);
+  p.out_ids = static_cast<uint32_t*>(out_ids);
+  p.out_scores = static_cast<float*>(out_scores);
+  p.rows = (uint32_t)rows;
+  p.hidden_size = (uint32_t)hidden_size;
+  p.vocab = (uint32_t)vocab;
+  split_workspace(workspace, rows, p);
+
+  const bool fast = fast_path(hidden, embedding, hidden_size);
+  DeviceInfo& d = device_info();
+  const int64_t max_blocks = (int64_t)d.sms * d.blocks_per_sm[0][fast ? 1 : 0];
+  // at least 8 candidates per group so tiny batches do not launch idle blocks
+  int64_t blocks = (p.total + (int64_t)kGroupsPerBlock * 8 - 1) / ((int64_t)kGroupsPerBlock * 8);
+  blocks = blocks < 1 ? 1 : (blocks > max_blocks ? max_blocks : blocks);
+  const int64_t groups = blocks * kGroupsPerBlock;
+  int64_t chunk = (p.total + groups - 1) / groups;
+  if (chunk < 1) chunk = 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fast)
+    ragged_head_kernel<RowMode::kCsr, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+  else
+    ragged_head_kernel<RowMode::kCsr, false><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+  return launch_status(cudaGetLastError());
+}
+
+namespace {
+
+mf_status dfa_validate(const void* hidden, uint64_t hidden_bytes, const void* embedding,
+                       uint64_t embedding_bytes, const void* state_offsets,
+                       uint64_t state_offsets_bytes, const void* arc_tokens,
+                       uint64_t arc_tokens_bytes, const void* arc_next, uint64_t arc_next_bytes,
+                       uint64_t steps, uint64_t batch, uint64_t num_states, uint64_t hidden_size,
+                       uint64_t vocab, void* stream) {
+  if (batch == 0 || num_states == 0 || hidden_size == 0 || vocab == 0 || steps == 0 ||
+      stream == nullptr)
+    return fail(MF_INVALID_ARGUMENT);
+  if (vocab > UINT32_MAX || num_states > (uint64_t)INT32_MAX - 1 || hidden_size > UINT32_MAX ||
+      batch > (uint64_t)kMaxDfaBatch)
+    return fail(MF_RESOURCE_LIMIT);
+  uint64_t hb, eb;
+  if (!mul_ok(batch, hidden_size, &hb) || !mul_ok(hb, 2, &hb) || !mul_ok(hb, steps, &hb) ||
+      !mul_ok(vocab, hidden_size, &eb) || !mul_ok(eb, 2, &eb))
+    return fail(MF_ARITHMETIC_OVERFLOW);
+  if (hidden_bytes != hb || embedding_bytes != eb || state_offsets_bytes != (num_states + 1) * 4 ||
+      arc_tokens_bytes == 0 || arc_tokens_bytes % 4 != 0 || arc_next_bytes != arc_tokens_bytes ||
+      arc_tokens_bytes / 4 > (uint64_t)INT32_MAX)
+    return fail(MF_INVALID_ARGUMENT);
+  if (!distinct({hidden, embedding, state_offsets, arc_tokens, arc_next}))
+    return fail(MF_INVALID_ARGUMENT);
+  return ok();
+}
+
+cudaError_t dfa_launch(RaggedParams p, bool fast, cudaStream_t s) {
+  DeviceInfo& d = device_info();
+  const int64_t blocks = (int64_t)d.sms * d.blocks_per_sm[1][fast ? 1 : 0];
+  const size_t smem = (p.rows + 1) * sizeof(int32_t);
+  // (kMaxDfaBatch + 1) * 4 bytes stays under the default 48 KB limit
+  if (fast)
+    ragged_head_kernel<RowMode::kDfa, true><<<(unsigned)blocks, kThreads, smem, s>>>(p, 0);
+  else
+    ragged_head_kernel<RowMode::kDfa, false><<<(unsigned)blocks, kThreads, smem, s>>>(p, 0);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" mf_status mf_dfa_head_step_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* state_offsets, uint64_t state_offsets_bytes, const void* arc_tokens,
+    uint64_t arc_tokens_bytes, const void* arc_next, uint64_t arc_next_bytes,
+    const void* states_in, uint64_t states_in_bytes, void* states_out, uint64_t states_out_bytes,
+    void* out_tokens, uint64_t out_tokens_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t batch, uint64_t num_states,
+    uint64_t hidden_size, uint64_t vocab, void* stream) {
+  mf_status st = dfa_validate(hidden, hidden_bytes, embedding, embedding_bytes, state_offsets,
+                              state_offsets_bytes, arc_tokens, arc_tokens_bytes, arc_next,
+                              arc_next_bytes, 1, batch, num_states, hidden_size, vocab, stream);
+  if (st.code != MF_OK) return st;
+  if (states_in_bytes != batch * 4 || states_out_bytes != batch * 4 ||
+      out_tokens_bytes != batch * 4 || (out_scores && out_scores_bytes != batch * 4) ||
+      workspace_bytes < mf_dfa_workspace_bytes(batch) ||
+      !distinct({states_in, states_out, out_tokens, workspace, hidden, embedding}) ||
+      (out_scores && !distinct({out_scores, states_in, states_out, out_tokens, workspace})))
+    return fail(MF_INVALID_ARGUMENT);
+  RaggedParams p{};
+  p.hidden = static_cast<const __half*>(hidden);
+  p.embedding = static_cast<const __half*>(embedding);
+  p.ids = static_cast<const int32_t*>(arc_tokens);
+  p.state_offsets = static_cast<const int32_t*>(state_offsets);
+  p.arc_next = static_cast<const uint32_t*>(arc_next);
+  p.states_in = static_cast<const uint32_t*>(states_in);
+  p.states_out = static_cast<uint32_t*>(states_out);
+  p.num_states = (uint32_t)num_states;
+  p.num_arcs = (int64_t)(arc_tokens_bytes / 4);
+  p.out_ids = static_cast<uint32_t*>(out_tokens);
+  p.out_scores = static_cast<float*>(out_scores);
+  p.rows = (uint32_t)batch;
+  p.hidden_size = (uint32_t)hidden_size;
+  p.vocab = (uint32_t)vocab;
+  split_workspace(workspace, batch, p);
+  return launch_status(dfa_launch(p, fast_path(hidden, embedding, hidden_size),
+                                  static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" mf_status mf_dfa_decode_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* state_offsets, uint64_t state_offsets_bytes, const void* arc_tokens,
+    uint64_t arc_tokens_bytes, const void* arc_next, uint64_t arc_next_bytes, void* state_trace,
+    uint64_t state_trace_bytes, void* token_trace, uint64_t token_trace_bytes, void* score_trace,
+    uint64_t score_trace_bytes, void* workspace, uint64_t workspace_bytes, uint64_t steps,
+    uint64_t batch, uint64_t num_states, uint64_t hidden_size, uint64_t vocab, void* stream) {
+  mf_status st = dfa_validate(hidden, hidden_bytes, embedding, embedding_bytes, state_offsets,
+                              state_offsets_bytes, arc_tokens, arc_tokens_bytes, arc_next,
+                              arc_next_bytes, steps, batch, num_states, hidden_size, vocab, stream);
+  if (st.code != MF_OK) return st;
+  uint64_t tb;
+  if (!mul_ok(steps, batch, &tb) || !mul_ok(tb, 4, &tb)) return fail(MF_ARITHMETIC_OVERFLOW);
+  if (state_trace_bytes != tb + batch * 4 || token_trace_bytes != tb ||
+      (score_trace && score_trace_bytes != tb) || workspace_bytes < mf_dfa_workspace_bytes(batch) ||
+      !distinct({state_trace, token_trace, workspace, hidden, embedding}) ||
+      (score_trace && !distinct({score_trace, state_trace, token_trace, workspace})))
+    return fail(MF_INVALID_ARGUMENT);
+  const bool fast = fast_path(hidden, embedding, hidden_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (uint64_t step = 0; step < steps; ++step) {
+    RaggedParams p{};
+    p.hidden = static_cast<const __half*>(hidden) + step * batch * hidden_size;
+    p.embedding = static_cast<const __half*>(embedding);
+    p.ids = static_cast<const int32_t*>(arc_tokens);
+    p.state_offsets = static_cast<const int32_t*>(state_offsets);
+    p.arc_next = static_cast<const uint32_t*>(arc_next);
+    p.states_in = static_cast<const uint32_t*>(state_trace) + step * batch;
+    p.states_out = static_cast<uint32_t*>(state_trace) + (step + 1) * batch;
+    p.num_states = (uint32_t)num_states;
+    p.num_arcs = (int64_t)(arc_tokens_bytes / 4);
+    p.out_ids = static_cast<uint32_t*>(token_trace) + step * batch;
+    p.out_scores = score_trace ? static_cast<float*>(score_trace) + step * batch : nullptr;
+    p.rows = (uint32_t)batch;
+    p.hidden_size = (uint32_t)hidden_size;
+    p.vocab = (uint32_t)vocab;
+    split_workspace(workspace, batch, p);
+    const cudaError_t e = dfa_launch(p, fast, s);
+    if (e != cudaSuccess) return launch_status(e);
+  }
+  return ok();
+}

@@ -1,0 +1,309 @@
+"""Host-side mirror of the reference's ``marketforge::cuda`` head interface.
+
+Same names, argument meaning and error behaviour as
+``include/marketforge/cuda/greedy.hpp`` (plus the boundary types of
+``device_buffer.hpp`` / ``cuda_stream.hpp`` / ``core/status.hpp``), calling
+the CUDA kernels through the C-ABI in ``include/mf_head.h``.  Buffers may be
+:class:`DeviceBuffer` objects or CUDA ``torch.Tensor`` s (their byte size is
+``numel * element_size``); streams may be :class:`CudaStream`,
+``torch.cuda.Stream`` or a raw ``cudaStream_t`` integer.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+from dataclasses import dataclass
+from typing import Optional, Union
+
+from ._lib import lib
+
+INVALID_TOKEN_ID = 0xFFFFFFFF
+"""``restricted_greedy_invalid_token_id`` (greedy.hpp:11-12)."""
+
+
+class ErrorCode(enum.IntEnum):
+    """``marketforge::ErrorCode`` (include/marketforge/core/status.hpp:7-31)."""
+
+    ok = 0
+    invalid_argument = 1
+    unsupported_dtype = 2
+    invalid_shape = 3
+    invalid_model = 4
+    arithmetic_overflow = 5
+    invalid_alignment = 6
+    allocation_failed = 7
+    insufficient_memory = 8
+    insufficient_resources = 9
+    io_error = 10
+    invalid_format = 11
+    invalid_utf8 = 12
+    invalid_json = 13
+    duplicate_key = 14
+    resource_limit = 15
+    truncated_data = 16
+    invalid_tensor = 17
+    missing_tensor = 18
+    unexpected_tensor = 19
+    hash_mismatch = 20
+    cuda_backend_failure = 21
+    cuda_runtime_failure = 22
+
+
+@dataclass(frozen=True)
+class Status:
+    """``marketforge::Status`` (status.hpp:33-49)."""
+
+    code: ErrorCode = ErrorCode.ok
+    detail: int = 0
+
+    def ok(self) -> bool:
+        return self.code == ErrorCode.ok
+
+    @staticmethod
+    def success() -> "Status":
+        return Status()
+
+    @staticmethod
+    def failure(code: ErrorCode, detail: int = 0) -> "Status":
+        return Status(ErrorCode(code), detail)
+
+
+def _status(s) -> Status:
+    return Status(ErrorCode(s.code), int(s.detail))
+
+
+class CudaStream:
+    """``marketforge::cuda::CudaStream`` (cuda_stream.hpp:19-41): a
+    non-blocking stream (src/cuda/cuda_stream.cu:13)."""
+
+    def __init__(self, stream=None):
+        import torch
+
+        self._stream = stream if stream is not None else torch.cuda.Stream()
+
+    @staticmethod
+    def create() -> "CudaStream":
+        return CudaStream()
+
+    def handle(self) -> int:
+        return int(self._stream.cuda_stream)
+
+    @property
+    def torch_stream(self):
+        return self._stream
+
+    def synchronize(self) -> Status:
+        self._stream.synchronize()
+        return Status.success()
+
+
+class DeviceBuffer:
+    """``marketforge::cuda::DeviceBuffer`` (device_buffer.hpp:20-56): an exact
+    byte-sized device allocation (torch's caching allocator underneath)."""
+
+    def __init__(self, tensor=None):
+        self._t = tensor
+
+    @staticmethod
+    def allocate(byte_count: int) -> "DeviceBuffer":
+        import torch
+
+        if byte_count == 0:
+            return DeviceBuffer()
+        return DeviceBuffer(torch.empty(int(byte_count), dtype=torch.uint8, device="cuda"))
+
+    def size_bytes(self) -> int:
+        return 0 if self._t is None else self._t.numel() * self._t.element_size()
+
+    def address(self) -> int:
+        return 0 if self._t is None else int(self._t.data_ptr())
+
+    @property
+    def tensor(self):
+        return self._t
+
+    def view(self, dtype):
+        return self._t.view(dtype)
+
+    def copy_from_host_async(self, source, byte_count: int, offset: int, stream) -> Status:
+        return _copy(self, source, byte_count, offset, stream, to_device=True)
+
+    def copy_to_host_async(self, destination, byte_count: int, offset: int, stream) -> Status:
+        return _copy(self, destination, byte_count, offset, stream, to_device=False)
+
+
+def _copy(buf: DeviceBuffer, host, byte_count, offset, stream, to_device) -> Status:
+    # src/cuda/device_buffer.cu:13-31 validation order
+    import torch
+
+    h = _stream_handle(stream)
+    if h == 0 or (byte_count != 0 and host is None):
+        return Status.failure(ErrorCode.invalid_argument)
+    if offset + byte_count > buf.size_bytes():
+        return Status.failure(ErrorCode.invalid_argument)
+    if byte_count == 0:
+        return Status.success()
+    host_t = host if isinstance(host, torch.Tensor) else torch.from_numpy(host)
+    host_bytes = host_t.reshape(-1).view(torch.uint8)[:byte_count]
+    dev = buf.tensor[offset:offset + byte_count]
+    with torch.cuda.stream(_torch_stream(stream)):
+        if to_device:
+            dev.copy_(host_bytes, non_blocking=True)
+        else:
+            host_bytes.copy_(dev, non_blocking=True)
+    return Status.success()
+
+
+Buffer = Union[DeviceBuffer, "torch.Tensor", None]  # noqa: F821
+
+
+def _addr(b: Buffer) -> int:
+    if b is None:
+        return 0
+    if isinstance(b, DeviceBuffer):
+        return b.address()
+    return int(b.data_ptr())
+
+
+def _size(b: Buffer) -> int:
+    if b is None:
+        return 0
+    if isinstance(b, DeviceBuffer):
+        return b.size_bytes()
+    return b.numel() * b.element_size()
+
+
+def _stream_handle(s) -> int:
+    if s is None:
+        return 0
+    if isinstance(s, CudaStream):
+        return s.handle()
+    if isinstance(s, int):
+        return s
+    return int(s.cuda_stream)
+
+
+def _torch_stream(s):
+    import torch
+
+    if isinstance(s, CudaStream):
+        return s.torch_stream
+    if isinstance(s, int):
+        return torch.cuda.ExternalStream(s)
+    return s
+
+
+def _pb(b: Buffer):
+    return ctypes.c_void_p(_addr(b) or None), ctypes.c_uint64(_size(b))
+
+
+def _sp(s):
+    h = _stream_handle(s)
+    return ctypes.c_void_p(h or None)
+
+
+# ---- reference-signature functions (greedy.hpp:17-49) ----------------------
+
+def greedy_select_f16(logits: Buffer, token_ids: Buffer, rows: int, vocabulary_size: int,
+                      stream) -> Status:
+    """greedy.hpp:17-21: argmax per row of fp16 logits[rows, V]."""
+    return _status(lib.mf_greedy_select_f16(*_pb(logits), *_pb(token_ids), rows,
+                                            vocabulary_size, _sp(stream)))
+
+
+def restricted_greedy_select_f16(logits: Buffer, allowed_token_ids: Buffer,
+                                 allowed_token_counts: Buffer, token_ids: Buffer, rows: int,
+                                 vocabulary_size: int, maximum_allowed_tokens: int,
+                                 stream) -> Status:
+    """greedy.hpp:29-33: masked argmax over a padded candidate table."""
+    return _status(lib.mf_restricted_greedy_select_f16(
+        *_pb(logits), *_pb(allowed_token_ids), *_pb(allowed_token_counts), *_pb(token_ids),
+        rows, vocabulary_size, maximum_allowed_tokens, _sp(stream)))
+
+
+def restricted_output_head_f16(hidden: Buffer, embedding: Buffer, allowed_token_ids: Buffer,
+                               allowed_token_counts: Buffer, token_ids: Buffer, rows: int,
+                               hidden_size: int, vocabulary_size: int,
+                               maximum_allowed_tokens: int, stream) -> Status:
+    """greedy.hpp:43-49: fused tied projection + restricted argmax."""
+    return _status(lib.mf_restricted_output_head_f16(
+        *_pb(hidden), *_pb(embedding), *_pb(allowed_token_ids), *_pb(allowed_token_counts),
+        *_pb(token_ids), rows, hidden_size, vocabulary_size, maximum_allowed_tokens,
+        _sp(stream)))
+
+
+# ---- ragged CSR head and device DFA (new batched launch path) -------------
+
+def head_workspace_bytes(rows: int) -> int:
+    return int(lib.mf_head_workspace_bytes(rows))
+
+
+def restricted_output_head_csr_f16(hidden: Buffer, embedding: Buffer, offsets: Buffer,
+                                   ids: Buffer, token_ids: Buffer, scores: Optional[Buffer],
+                                   workspace: Buffer, rows: int, hidden_size: int,
+                                   vocabulary_size: int, stream) -> Status:
+    """Ragged head: row r's candidates are ids[offsets[r]:offsets[r+1]]."""
+    return _status(lib.mf_head_restricted_csr_f16(
+        *_pb(hidden), *_pb(embedding), *_pb(offsets), *_pb(ids), *_pb(token_ids), *_pb(scores),
+        *_pb(workspace), rows, hidden_size, vocabulary_size, _sp(stream)))
+
+
+def dfa_head_step_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer,
+                      arc_tokens: Buffer, arc_next: Buffer, states_in: Buffer,
+                      states_out: Buffer, tokens: Buffer, scores: Optional[Buffer],
+                      workspace: Buffer, batch: int, num_states: int, hidden_size: int,
+                      vocabulary_size: int, stream) -> Status:
+    """One device step: allowed-set lookup, restricted head, DFA advance."""
+    return _status(lib.mf_dfa_head_step_f16(
+        *_pb(hidden), *_pb(embedding), *_pb(state_offsets), *_pb(arc_tokens), *_pb(arc_next),
+        *_pb(states_in), *_pb(states_out), *_pb(tokens), *_pb(scores), *_pb(workspace),
+        batch, num_states, hidden_size, vocabulary_size, _sp(stream)))
+
+
+def dfa_decode_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer, arc_tokens: Buffer,
+                   arc_next: Buffer, state_trace: Buffer, token_trace: Buffer,
+                   score_trace: Optional[Buffer], workspace: Buffer, steps: int, batch: int,
+                   num_states: int, hidden_size: int, vocabulary_size: int, stream) -> Status:
+    """``steps`` DFA head steps back to back, no host synchronisation."""
+    return _status(lib.mf_dfa_decode_f16(
+        *_pb(hidden), *_pb(embedding), *_pb(state_offsets), *_pb(arc_tokens), *_pb(arc_next),
+        *_pb(state_trace), *_pb(token_trace), *_pb(score_trace), *_pb(workspace), steps, batch,
+        num_states, hidden_size, vocabulary_size, _sp(stream)))
+
+
+class RaggedHead:
+    """Owns the workspace for repeated ragged-head calls on one stream.
+
+    ``embedding`` stays resident; each ``__call__`` takes a batch of hidden
+    rows and its CSR allowed sets (device tensors) and returns
+    ``(token_ids, scores)`` device tensors.
+    """
+
+    def __init__(self, embedding, max_rows: int, stream=None):
+        import torch
+
+        self.embedding = embedding
+        self.vocab, self.hidden_size = int(embedding.shape[0]), int(embedding.shape[1])
+        self.max_rows = int(max_rows)
+        self.workspace = torch.zeros(head_workspace_bytes(self.max_rows), dtype=torch.uint8,
+                                     device=embedding.device)
+        self.stream = stream
+
+    def __call__(self, hidden, offsets, ids, out_ids=None, out_scores=None):
+        import torch
+
+        rows = int(hidden.shape[0])
+        if rows > self.max_rows:
+            raise ValueError(f"batch of {rows} rows exceeds max_rows={self.max_rows}")
+        if out_ids is None:
+            out_ids = torch.empty(rows, dtype=torch.int32, device=hidden.device)
+        if out_scores is None:
+            out_scores = torch.empty(rows, dtype=torch.float32, device=hidden.device)
+        ws = self.workspace[: head_workspace_bytes(rows)]
+        stream = self.stream if self.stream is not None else torch.cuda.current_stream()
+        st = restricted_output_head_csr_f16(hidden, self.embedding, offsets, ids, out_ids,
+                                            out_scores, ws, rows, self.hidden_size, self.vocab,
+                                            stream)
+        if not st.ok():
+            raise RuntimeError(f"restricted head failed: {st}")
+        return out_ids, out_scores

@@ -1,0 +1,259 @@
+"""ctypes wrapper of the CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+Loads ``oracle/liboracle.so`` (oracle.c, the C restatement of the
+reference's CPU path) and, when it was built, ``oracle/_ref/libmfref.so``
+(the reference's own CPU sources).  Only tests/, ``__graft_entry__.smoke``
+and bench.py's CPU-baseline / reference legs use this module, and only as a
+checker or a timed CPU baseline; the product never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+REF_LIB = os.path.join(HERE, "_ref", "libmfref.so")
+INVALID = 0xFFFFFFFF
+
+_P = ctypes.c_void_p
+_U64 = ctypes.c_uint64
+
+
+def build(ref: bool = False) -> None:
+    """Compile the oracle (and the reference CPU library when asked and the
+    reference sources are present)."""
+    targets = ["all"]
+    if ref and os.path.isdir(os.environ.get("REF", "/root/reference")):
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+
+
+def _load():
+    if not os.path.exists(LIB):
+        build()
+    lib = ctypes.CDLL(LIB)
+    lib.orc_half_to_float.argtypes = [ctypes.c_uint16]
+    lib.orc_half_to_float.restype = ctypes.c_float
+    lib.orc_splitmix64.argtypes = [_U64]
+    lib.orc_splitmix64.restype = _U64
+    lib.orc_dfa_next.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
+    lib.orc_dfa_next.restype = ctypes.c_uint32
+    for name, args in {
+        "orc_half_to_float_array": [_P, _P, _U64],
+        "orc_rms_norm_f32": [_P, _P, _U64, _U64, ctypes.c_float, _P],
+        "orc_linear_f32": [_P, _P, _U64, _U64, _U64, _P],
+        "orc_restricted_head_csr": [_P, _P, _P, _P, _U64, _U64, _U64, _P, _P, _P, ctypes.c_int],
+        "orc_full_logits_masked_head_csr": [_P, _P, _P, _P, _U64, _U64, _U64, _P, _P, ctypes.c_int],
+        "orc_greedy_select_f16": [_P, _U64, _U64, _P],
+        "orc_restricted_greedy_select_f16": [_P, _P, _P, _U64, _U64, _U64, _P],
+        "orc_restricted_head_padded": [_P, _P, _P, _P, _U64, _U64, _U64, _U64, _P, _P],
+        "orc_dense_head": [_P, _P, _U64, _U64, _U64, _U64, _P, _P, _P],
+        "orc_dfa_decode": [_P, _P, _P, _P, _P, ctypes.c_uint32, _P, _U64, _U64, _U64, _U64, _P, _P],
+    }.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = None
+    return lib
+
+
+lib = _load()
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def widen(h: np.ndarray) -> np.ndarray:
+    """fp16 -> fp32 by the oracle's own exact conversion."""
+    h = np.ascontiguousarray(h, dtype=np.float16)
+    out = np.empty(h.shape, dtype=np.float32)
+    lib.orc_half_to_float_array(_p(h.view(np.uint16)), _p(out), h.size)
+    return out
+
+
+def rms_norm_f32(x, w, eps=1e-5):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    rows = x.size // w.size
+    lib.orc_rms_norm_f32(_p(x), _p(w), rows, w.size, eps, _p(out))
+    return out
+
+
+def linear_f32(x, w):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty((x.shape[0], w.shape[0]), np.float32)
+    lib.orc_linear_f32(_p(x), _p(w), x.shape[0], x.shape[1], w.shape[0], _p(out))
+    return out
+
+
+def restricted_head_csr(hidden_f16, emb_f16, offsets, ids, threads=1):
+    """-> (ids u32[rows], best f32[rows], runner_up f32[rows])."""
+    hidden = widen(hidden_f16)
+    emb = np.ascontiguousarray(emb_f16, np.float16)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    rows = hidden.shape[0]
+    out = np.empty(rows, np.uint32)
+    best = np.empty(rows, np.float32)
+    ru = np.empty(rows, np.float32)
+    lib.orc_restricted_head_csr(_p(hidden), _p(emb.view(np.uint16)), _p(offsets), _p(ids), rows,
+                                hidden.shape[1], emb.shape[0], _p(out), _p(best), _p(ru), threads)
+    return out, best, ru
+
+
+def full_logits_masked_head_csr(hidden_f16, emb_f16, offsets, ids, threads=1):
+    hidden = widen(hidden_f16)
+    emb = np.ascontiguousarray(emb_f16, np.float16)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    rows = hidden.shape[0]
+    out = np.empty(rows, np.uint32)
+    best = np.empty(rows, np.float32)
+    lib.orc_full_logits_masked_head_csr(_p(hidden), _p(emb.view(np.uint16)), _p(offsets), _p(ids),
+                                        rows, hidden.shape[1], emb.shape[0], _p(out), _p(best),
+                                        threads)
+    return out, best
+
+
+def restricted_head_padded(hidden_f16, emb_f16, allowed, counts, max_allowed):
+    hidden = widen(hidden_f16)
+    emb = np.ascontiguousarray(emb_f16, np.float16)
+    allowed = np.ascontiguousarray(allowed, np.uint32)
+    counts = np.ascontiguousarray(counts, np.uint32)
+    rows = hidden.shape[0]
+    out = np.empty(rows, np.uint32)
+    best = np.empty(rows, np.float32)
+    lib.orc_restricted_head_padded(_p(hidden), _p(emb.view(np.uint16)), _p(allowed), _p(counts),
+                                   rows, hidden.shape[1], emb.shape[0], max_allowed, _p(out),
+                                   _p(best))
+    return out, best
+
+
+def greedy_select_f16(logits_f16):
+    lg = np.ascontiguousarray(logits_f16, np.float16)
+    out = np.empty(lg.shape[0], np.uint32)
+    lib.orc_greedy_select_f16(_p(lg.view(np.uint16)), lg.shape[0], lg.shape[1], _p(out))
+    return out
+
+
+def restricted_greedy_select_f16(logits_f16, allowed, counts, max_allowed):
+    lg = np.ascontiguousarray(logits_f16, np.float16)
+    allowed = np.ascontiguousarray(allowed, np.uint32)
+    counts = np.ascontiguousarray(counts, np.uint32)
+    out = np.empty(lg.shape[0], np.uint32)
+    lib.orc_restricted_greedy_select_f16(_p(lg.view(np.uint16)), _p(allowed), _p(counts),
+                                         lg.shape[0], lg.shape[1], max_allowed, _p(out))
+    return out
+
+
+def dense_head(hidden_f16, emb_f16, vocab_begin=0, vocab_end=None):
+    hidden = widen(hidden_f16)
+    emb = np.ascontiguousarray(emb_f16, np.float16)
+    vocab_end = emb.shape[0] if vocab_end is None else vocab_end
+    rows = hidden.shape[0]
+    out = np.empty(rows, np.uint32)
+    best = np.empty(rows, np.float32)
+    ru = np.empty(rows, np.float32)
+    lib.orc_dense_head(_p(hidden), _p(emb.view(np.uint16)), rows, hidden.shape[1], vocab_begin,
+                       vocab_end, _p(out), _p(best), _p(ru))
+    return out, best, ru
+
+
+def dfa_decode(hidden_f16, emb_f16, dfa_offsets, dfa_ids, num_states, init_states, arc_next=None):
+    """hidden_f16 [steps, batch, H] -> (tokens [steps, batch], states [steps+1, batch]).
+    arc_next None = the synthetic hash transition, else the per-arc table."""
+    steps, batch, h = hidden_f16.shape
+    hidden = widen(hidden_f16)
+    emb = np.ascontiguousarray(emb_f16, np.float16)
+    off = np.ascontiguousarray(dfa_offsets, np.int32)
+    ids = np.ascontiguousarray(dfa_ids, np.int32)
+    init = np.ascontiguousarray(init_states, np.uint32)
+    tokens = np.empty((steps, batch), np.uint32)
+    states = np.empty((steps + 1, batch), np.uint32)
+    nxt = None if arc_next is None else np.ascontiguousarray(arc_next, np.uint32)
+    lib.orc_dfa_decode(_p(hidden), _p(emb.view(np.uint16)), _p(off), _p(ids),
+                       None if nxt is None else _p(nxt), num_states,
+                       _p(init), steps, batch, h, emb.shape[0], _p(tokens), _p(states))
+    return tokens, states
+
+
+# ---- the reference's own CPU code (oracle/_ref), when built --------------
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB)
+
+
+_ref = None
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise RuntimeError(f"{REF_LIB} not built (make -C oracle ref)")
+        r = ctypes.CDLL(REF_LIB)
+        r.mfref_rms_norm_f32.argtypes = [_P, _P, _U64, _U64, ctypes.c_float, _P]
+        r.mfref_linear_f32.argtypes = [_P, _P, _U64, _U64, _U64, _P]
+        r.mfref_full_logits_masked_head_csr.argtypes = [_P, _P, _P, _P, _U64, _U64, _U64, _P, _P,
+                                                        ctypes.c_int]
+        r.mfref_market_dfa.argtypes = [_P, _P, _P, _P, _P, _P]
+        r.mfref_market_dfa_advance.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
+        r.mfref_market_dfa_advance.restype = ctypes.c_uint32
+        for f in ("mfref_rms_norm_f32", "mfref_linear_f32", "mfref_full_logits_masked_head_csr",
+                  "mfref_market_dfa"):
+            getattr(r, f).restype = ctypes.c_int
+        _ref = r
+    return _ref
+
+
+def ref_linear_f32(x, w):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty((x.shape[0], w.shape[0]), np.float32)
+    code = ref_lib().mfref_linear_f32(_p(x), _p(w), x.shape[0], x.shape[1], w.shape[0], _p(out))
+    assert code == 0, code
+    return out
+
+
+def ref_rms_norm_f32(x, w, eps=1e-5):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    code = ref_lib().mfref_rms_norm_f32(_p(x), _p(w), x.size // w.size, w.size, eps, _p(out))
+    assert code == 0, code
+    return out
+
+
+def ref_full_logits_masked_head_csr(hidden_f16, emb_f32, offsets, ids, threads=1):
+    hidden = widen(hidden_f16)
+    emb_f32 = np.ascontiguousarray(emb_f32, np.float32)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    rows = hidden.shape[0]
+    out = np.empty(rows, np.uint32)
+    best = np.empty(rows, np.float32)
+    code = ref_lib().mfref_full_logits_masked_head_csr(
+        _p(hidden), _p(emb_f32), _p(offsets), _p(ids), rows, hidden.shape[1], emb_f32.shape[0],
+        _p(out), _p(best), threads)
+    assert code == 0, code
+    return out, best
+
+
+def ref_market_dfa():
+    """The reference's SmolLM2 market-action DFA as CSR numpy arrays."""
+    r = ref_lib()
+    ns, na = ctypes.c_uint32(), ctypes.c_uint32()
+    assert r.mfref_market_dfa(ctypes.byref(ns), ctypes.byref(na), None, None, None, None) == 0
+    off = np.empty(ns.value + 1, np.int32)
+    tok = np.empty(na.value, np.uint32)
+    nxt = np.empty(na.value, np.uint32)
+    term = np.empty(ns.value, np.uint8)
+    assert r.mfref_market_dfa(ctypes.byref(ns), ctypes.byref(na), _p(off), _p(tok), _p(nxt),
+                              _p(term)) == 0
+    return off, tok, nxt, term

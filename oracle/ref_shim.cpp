@@ -1,0 +1,165 @@
+// C-ABI shim over the reference's own CPU code — TEST INFRASTRUCTURE ONLY.
+//
+// Compiled by oracle/Makefile together with the reference's unmodified
+// sources (src/cpu/operators.cpp, src/core/shape.cpp, src/grammar/*.cpp)
+// into oracle/_ref/libmfref.so.  Tests use it to pin oracle/oracle.c bit for
+// bit against the reference, and bench.py's reference arm times
+// mfref_full_logits_masked_head_csr on the host cores.  Nothing in the
+// product links or loads it.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <limits>
+#include <thread>
+#include <vector>
+
+#include "marketforge/core/shape.hpp"
+#include "marketforge/core/tensor_view.hpp"
+#include "marketforge/cpu/operators.hpp"
+#include "marketforge/grammar/smollm2_market_actions.hpp"
+
+namespace {
+
+using marketforge::ConstTensorView;
+using marketforge::DType;
+using marketforge::MemoryKind;
+using marketforge::TensorView;
+
+marketforge::Shape shape2(std::uint64_t a, std::uint64_t b) {
+  const std::uint64_t e[2] = {a, b};
+  return marketforge::make_shape(std::span<const std::uint64_t>(e, 2)).value();
+}
+marketforge::Shape shape1(std::uint64_t a) {
+  const std::uint64_t e[1] = {a};
+  return marketforge::make_shape(std::span<const std::uint64_t>(e, 1)).value();
+}
+
+constexpr std::uint32_t kInvalid = UINT32_MAX;
+
+// Masked argmax over one row of logits with the restricted head's rules
+// (include/marketforge/cuda/greedy.hpp:35-42).  Written here, not taken from
+// the reference: the reference's CPU model only does the full argmax.
+void masked_pick(const float* logits, const std::int32_t* ids, std::int32_t n,
+                 std::uint64_t vocab, std::uint32_t* out_id, float* out_best) {
+  bool invalid = n <= 0;
+  for (std::int32_t k = 0; k < n && !invalid; ++k)
+    if (ids[k] < 0 || static_cast<std::uint64_t>(ids[k]) >= vocab) invalid = true;
+  std::uint32_t best_id = kInvalid, fallback = kInvalid;
+  float best = -std::numeric_limits<float>::infinity();
+  if (!invalid) {
+    for (std::int32_t k = 0; k < n; ++k) {
+      const auto t = static_cast<std::uint32_t>(ids[k]);
+      fallback = t < fallback ? t : fallback;
+      const float v = logits[t];
+      if (v > best || (v == best && t < best_id)) {
+        best = v;
+        best_id = t;
+      }
+    }
+  }
+  *out_id = invalid ? kInvalid : (best_id != kInvalid ? best_id : fallback);
+  if (out_best) *out_best = (invalid || best_id == kInvalid) ? NAN : best;
+}
+
+} // namespace
+
+extern "C" {
+
+// marketforge::rms_norm_f32 (src/cpu/operators.cpp:489).  Returns the
+// reference's ErrorCode (0 = ok).
+int mfref_rms_norm_f32(const float* x, const float* weight, std::uint64_t rows,
+                       std::uint64_t hidden, float eps, float* out) {
+  const auto s = marketforge::rms_norm_f32(
+      ConstTensorView{x, shape2(rows, hidden), DType::f32, MemoryKind::host},
+      ConstTensorView{weight, shape1(hidden), DType::f32, MemoryKind::host}, eps,
+      TensorView{out, shape2(rows, hidden), DType::f32, MemoryKind::host});
+  return static_cast<int>(s.code);
+}
+
+// marketforge::linear_f32 (src/cpu/operators.cpp:539).
+int mfref_linear_f32(const float* x, const float* w, std::uint64_t rows,
+                     std::uint64_t in_width, std::uint64_t out_width, float* out) {
+  const auto s = marketforge::linear_f32(
+      ConstTensorView{x, shape2(rows, in_width), DType::f32, MemoryKind::host},
+      ConstTensorView{w, shape2(out_width, in_width), DType::f32, MemoryKind::host},
+      TensorView{out, shape2(rows, out_width), DType::f32, MemoryKind::host});
+  return static_cast<int>(s.code);
+}
+
+// The reference CPU path for a ragged batch: per row, linear_f32 over every
+// vocab row of the FP32 embedding, then the masked argmax over the row's CSR
+// candidates.  Rows are split over `threads` std::threads.
+int mfref_full_logits_masked_head_csr(const float* hidden, const float* embedding_f32,
+                                      const std::int32_t* offsets, const std::int32_t* ids,
+                                      std::uint64_t rows, std::uint64_t hidden_size,
+                                      std::uint64_t vocab, std::uint32_t* out_ids,
+                                      float* out_best, int threads) {
+  if (threads < 1) threads = 1;
+  if (static_cast<std::uint64_t>(threads) > rows) threads = static_cast<int>(rows);
+  std::vector<int> codes(static_cast<std::size_t>(threads), 0);
+  auto work = [&](int t) {
+    std::vector<float> logits(vocab);
+    const std::uint64_t b = rows * t / threads, e = rows * (t + 1) / threads;
+    for (std::uint64_t r = b; r < e; ++r) {
+      const int code = mfref_linear_f32(hidden + r * hidden_size, embedding_f32, 1,
+                                        hidden_size, vocab, logits.data());
+      if (code != 0) {
+        codes[t] = code;
+        return;
+      }
+      masked_pick(logits.data(), ids + offsets[r], offsets[r + 1] - offsets[r], vocab,
+                  out_ids + r, out_best ? out_best + r : nullptr);
+    }
+  };
+  if (threads == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> pool;
+    for (int t = 0; t < threads; ++t) pool.emplace_back(work, t);
+    for (auto& th : pool) th.join();
+  }
+  for (int c : codes)
+    if (c != 0) return c;
+  return 0;
+}
+
+// Dumps the SmolLM2 market-action DFA (SmolLm2MarketActionCatalog::create,
+// src/grammar/smollm2_market_actions.cpp:42) as CSR: state s has arcs
+// [offsets[s], offsets[s+1]) with tokens[] and next[] in the order
+// ActionDfa::allowed returns them (sorted by token).  terminal[s] = 1 when
+// ActionDfa::terminal(s).  Call with null arrays to get the counts.
+int mfref_market_dfa(std::uint32_t* num_states, std::uint32_t* num_arcs,
+                     std::int32_t* offsets, std::uint32_t* tokens,
+                     std::uint32_t* next, std::uint8_t* terminal) {
+  auto catalog = marketforge::SmolLm2MarketActionCatalog::create();
+  if (!catalog) return static_cast<int>(catalog.status().code);
+  const auto& dfa = catalog.value().dfa();
+  *num_states = static_cast<std::uint32_t>(dfa.state_count());
+  *num_arcs = static_cast<std::uint32_t>(dfa.arc_count());
+  if (!offsets) return 0;
+  std::int32_t at = 0;
+  for (std::uint32_t s = 0; s < *num_states; ++s) {
+    offsets[s] = at;
+    const auto arcs = dfa.allowed(marketforge::GrammarState{s});
+    if (!arcs) return static_cast<int>(arcs.status().code);
+    for (const auto& arc : arcs.value()) {
+      tokens[at] = arc.token;
+      next[at] = arc.next.value;
+      ++at;
+    }
+    terminal[s] = dfa.terminal(marketforge::GrammarState{s}) ? 1 : 0;
+  }
+  offsets[*num_states] = at;
+  return 0;
+}
+
+// ActionDfa::advance (src/grammar/action_dfa.cpp:123-144) on the market DFA:
+// returns the next state, or UINT32_MAX when the token is not allowed.
+std::uint32_t mfref_market_dfa_advance(std::uint32_t state, std::uint32_t token) {
+  static auto catalog = marketforge::SmolLm2MarketActionCatalog::create();
+  if (!catalog) return kInvalid;
+  const auto r = catalog.value().dfa().advance(marketforge::GrammarState{state}, token);
+  return r ? r.value().value : kInvalid;
+}
+
+} // extern "C"

@@ -1,0 +1,157 @@
+"""CPU checks of the C-ABI library: it loads, exports every symbol that
+include/mf_head.h declares, and rejects bad metadata on the host before any
+CUDA call (no GPU is needed for those paths: pointers here are never
+dereferenced)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from market_sim_b200 import build
+
+    build.build()
+    from market_sim_b200 import _lib
+
+    return _lib
+
+
+def declared_symbols():
+    names = []
+    for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if h.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", h)).read()
+            names += re.findall(r"^MF_API\s+\w+\s+(mf_\w+)\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    declared = declared_symbols()
+    assert declared, "no MF_API declarations found"
+    out = subprocess.run(["nm", "-D", "--defined-only", lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(mf_\w+)$", out, flags=re.M))
+    missing = [n for n in declared if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    for n in declared:
+        assert hasattr(lib.lib, n)
+    assert set(lib.EXPORTED) <= set(declared) | set()
+
+
+def test_built_for_sm100a(lib):
+    assert lib.lib.mf_built_arch() == 1000
+    assert lib.lib.mf_version() >= 1
+
+
+def test_workspace_sizes(lib):
+    for rows in (1, 7, 256, 10_000):
+        b = lib.lib.mf_head_workspace_bytes(rows)
+        assert b >= rows * 12 + 16 and b % 16 == 0
+        assert lib.lib.mf_dfa_workspace_bytes(rows) == b
+
+
+FAKE = [0x10000 * (i + 1) for i in range(12)]  # distinct, 16-byte aligned, never dereferenced
+STREAM = 0xDEAD0
+
+
+def _p(i):
+    return ctypes.c_void_p(FAKE[i])
+
+
+def test_padded_head_rejections(lib):
+    """Validation order of src/cuda/greedy.cu:349-399."""
+    from market_sim_b200.head import ErrorCode as E
+
+    f = lib.lib.mf_restricted_output_head_f16
+    rows, hs, v, mx = 1, 4, 8, 2
+
+    def call(rows=rows, hs=hs, v=v, mx=mx, stream=STREAM, sizes=None, ptrs=None):
+        s = sizes or [rows * hs * 2, v * hs * 2, rows * mx * 4, rows * 4, rows * 4]
+        p = ptrs or [_p(0), _p(1), _p(2), _p(3), _p(4)]
+        return f(p[0], s[0], p[1], s[1], p[2], s[2], p[3], s[3], p[4], s[4], rows, hs, v, mx,
+                 ctypes.c_void_p(stream) if stream else None).code
+
+    assert call(rows=0) == E.invalid_argument
+    assert call(mx=0) == E.invalid_argument
+    assert call(hs=0) == E.invalid_argument
+    assert call(stream=0) == E.invalid_argument
+    assert call(rows=2**64 - 1) == E.resource_limit
+    assert call(v=2**32) == E.resource_limit
+    assert call(mx=2**32) == E.resource_limit
+    assert call(hs=2**62, sizes=[0, 0, 8, 4, 4]) == E.arithmetic_overflow
+    assert call(sizes=[rows * hs * 2 + 2, v * hs * 2, rows * mx * 4, 4, 4]) == E.invalid_argument
+    assert call(ptrs=[_p(0), _p(1), _p(2), _p(3), _p(3)]) == E.invalid_argument
+    assert call(ptrs=[_p(0), None, _p(2), _p(3), _p(4)]) == E.invalid_argument
+
+
+def test_csr_head_rejections(lib):
+    from market_sim_b200.head import ErrorCode as E
+
+    f = lib.lib.mf_head_restricted_csr_f16
+    rows, hs, v, total = 4, 576, 1000, 10
+    ws = lib.lib.mf_head_workspace_bytes(rows)
+
+    def call(rows=rows, hs=hs, v=v, stream=STREAM, sizes=None, ptrs=None, scores=True):
+        s = sizes or [rows * hs * 2, v * hs * 2, (rows + 1) * 4, total * 4, rows * 4, rows * 4, ws]
+        p = ptrs or [_p(i) for i in range(7)]
+        return f(p[0], s[0], p[1], s[1], p[2], s[2], p[3], s[3], p[4], s[4],
+                 p[5] if scores else None, s[5] if scores else 0, p[6], s[6], rows, hs, v,
+                 ctypes.c_void_p(stream) if stream else None).code
+
+    assert call(rows=0) == E.invalid_argument
+    assert call(stream=0) == E.invalid_argument
+    assert call(v=2**32) == E.resource_limit
+    assert call(rows=2**31) == E.resource_limit
+    assert call(sizes=[rows * hs * 2, v * hs * 2, rows * 4, total * 4, rows * 4, rows * 4, ws]) \
+        == E.invalid_argument  # offsets must hold rows + 1 entries
+    assert call(sizes=[rows * hs * 2, v * hs * 2, (rows + 1) * 4, total * 4 + 2, rows * 4, rows * 4,
+                       ws]) == E.invalid_argument
+    assert call(sizes=[rows * hs * 2, v * hs * 2, (rows + 1) * 4, total * 4, rows * 4, rows * 4,
+                       ws - 16]) == E.invalid_argument  # workspace too small
+    assert call(ptrs=[_p(0), _p(1), _p(2), _p(3), _p(4), _p(4), _p(6)]) == E.invalid_argument
+
+
+def test_dfa_rejections(lib):
+    from market_sim_b200.head import ErrorCode as E
+
+    f = lib.lib.mf_dfa_decode_f16
+    steps, batch, ns, hs, v, arcs = 3, 4, 5, 576, 1000, 9
+    ws = lib.lib.mf_dfa_workspace_bytes(batch)
+
+    def call(steps=steps, batch=batch, ns=ns, sizes=None):
+        s = sizes or [steps * batch * hs * 2, v * hs * 2, (ns + 1) * 4, arcs * 4, arcs * 4,
+                      (steps + 1) * batch * 4, steps * batch * 4, steps * batch * 4, ws]
+        p = [_p(i) for i in range(9)]
+        args = []
+        for i in range(9):
+            args += [p[i], s[i]]
+        return f(*args, steps, batch, ns, hs, v, ctypes.c_void_p(STREAM)).code
+
+    assert call(steps=0) == E.invalid_argument
+    assert call(batch=0) == E.invalid_argument
+    assert call(batch=8193, sizes=[steps * 8193 * hs * 2, v * hs * 2, (ns + 1) * 4, arcs * 4,
+                                   arcs * 4, (steps + 1) * 8193 * 4, steps * 8193 * 4,
+                                   steps * 8193 * 4, ws]) == E.resource_limit
+    assert call(sizes=[steps * batch * hs * 2, v * hs * 2, (ns + 1) * 4, arcs * 4, arcs * 4 - 4,
+                       (steps + 1) * batch * 4, steps * batch * 4, steps * batch * 4, ws]) \
+        == E.invalid_argument  # arc_next must match arc_tokens
+
+
+def test_greedy_rejections(lib):
+    from market_sim_b200.head import ErrorCode as E
+
+    f = lib.lib.mf_greedy_select_f16
+    st = ctypes.c_void_p(STREAM)
+    assert f(_p(0), 16, _p(1), 4, 0, 8, st).code == E.invalid_argument
+    assert f(_p(0), 16, _p(1), 4, 1, 8, None).code == E.invalid_argument
+    assert f(_p(0), 16, _p(1), 4, 1, 7, st).code == E.invalid_argument
+    assert f(_p(0), 16, _p(1), 4, 1, 2**32, st).code == E.resource_limit
+    assert f(_p(0), 16, _p(0), 4, 1, 8, st).code == E.invalid_argument

@@ -1,0 +1,369 @@
+"""GPU parity tests for the restricted head and the selection kernels, all
+through the C-ABI (market_sim_b200.head mirrors the reference's
+marketforge::cuda functions over it).  The known-answer cases restate the
+reference's own CUDA tests (tests/cuda/cuda_tests.cu); the seeded cases
+compare against the FP32 CPU oracle (oracle/oracle.c)."""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from helpers import INVALID, check_head_parity, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def mf(cuda):
+    from market_sim_b200 import head
+
+    return head
+
+
+@pytest.fixture(scope="module")
+def O():
+    from oracle import oracle
+
+    return oracle
+
+
+@pytest.fixture(scope="module")
+def emb_full(cuda):
+    from market_sim_b200 import synth
+
+    e = synth.embedding(20251201)
+    return e, to_dev(e)
+
+
+def _u32(t):
+    return t.cpu().numpy().view(np.uint32)
+
+
+def _stream():
+    import torch
+
+    return torch.cuda.current_stream()
+
+
+def _csr_call(mf, hidden, emb_dev, offsets, ids, vocab=None, hidden_size=None, ws=None):
+    import torch
+
+    rows = int(hidden.shape[0])
+    vocab = int(emb_dev.shape[0]) if vocab is None else vocab
+    hidden_size = int(hidden.shape[1]) if hidden_size is None else hidden_size
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+    if ws is None:
+        ws = torch.zeros(mf.head_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    ids_d = to_dev(ids) if ids.size else torch.empty(0, dtype=torch.int32, device="cuda")
+    st = mf.restricted_output_head_csr_f16(to_dev(hidden) if isinstance(hidden, np.ndarray) else hidden,
+                                           emb_dev, to_dev(offsets), ids_d, out, sc, ws, rows,
+                                           hidden_size, vocab, _stream())
+    assert st.ok(), st
+    torch.cuda.synchronize()
+    return _u32(out), sc.cpu().numpy(), ws
+
+
+# ---- known-answer tests from the reference --------------------------------
+
+def test_kat_head_3x8x17_padded(mf, golden_dir):
+    """tests/cuda/cuda_tests.cu:699-800 through restricted_output_head_f16."""
+    import torch
+
+    k = json.load(open(os.path.join(golden_dir, "kat_head_3x8x17.json")))
+    h = np.array(k["hidden_f16_bits"], np.uint16).view(np.float16)
+    e = np.array(k["embedding_f16_bits"], np.uint16).view(np.float16)
+    out = torch.empty(k["rows"], dtype=torch.int32, device="cuda")
+    st = mf.restricted_output_head_f16(to_dev(h), to_dev(e), to_dev(np.array(k["allowed"], np.uint32)),
+                                       to_dev(np.array(k["counts"], np.uint32)), out, k["rows"],
+                                       k["hidden_size"], k["vocabulary_size"], k["maximum_allowed"],
+                                       _stream())
+    assert st.ok(), st
+    assert _u32(out).tolist() == k["expected"]
+
+
+def test_kat_head_3x8x17_csr(mf, golden_dir):
+    k = json.load(open(os.path.join(golden_dir, "kat_head_3x8x17.json")))
+    h = np.array(k["hidden_f16_bits"], np.uint16).view(np.float16).reshape(k["rows"], -1)
+    e = np.array(k["embedding_f16_bits"], np.uint16).view(np.float16).reshape(k["vocabulary_size"], -1)
+    allowed = np.array(k["allowed"], np.int32).reshape(k["rows"], -1)
+    ids = np.concatenate([allowed[r, :c] for r, c in enumerate(k["counts"])]).astype(np.int32)
+    off = np.concatenate([[0], np.cumsum(k["counts"])]).astype(np.int32)
+    got, sc, ws = _csr_call(mf, h, to_dev(e), off, ids)
+    assert got.tolist() == k["expected"]
+    assert np.isnan(sc[2]) and not np.isnan(sc[:2]).any()
+    assert int(ws.sum()) == 0, "workspace must be left zero"
+
+
+def test_kat_invalid_rows_padded(mf, golden_dir):
+    """tests/cuda/cuda_tests.cu:1341-1404: count 0, count > max, id >= V."""
+    import torch
+
+    k = json.load(open(os.path.join(golden_dir, "kat_invalid_rows.json")))
+    rows, hs, v, mx = k["rows"], k["hidden_size"], k["vocabulary_size"], k["maximum_allowed"]
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    st = mf.restricted_output_head_f16(
+        torch.zeros(rows * hs, dtype=torch.float16, device="cuda"),
+        torch.zeros(v * hs, dtype=torch.float16, device="cuda"),
+        to_dev(np.array(k["allowed"], np.uint32)), to_dev(np.array(k["counts"], np.uint32)), out,
+        rows, hs, v, mx, _stream())
+    assert st.ok()
+    assert _u32(out).tolist() == k["expected"]
+
+
+def test_csr_invalid_rows(mf):
+    """CSR counterparts of the invalid-row cases: empty row, id >= V, id < 0."""
+    h = np.zeros((4, 2), np.float16)
+    e = np.ones((5, 2), np.float16)
+    off = np.array([0, 0, 2, 4, 5], np.int32)
+    ids = np.array([1, 5, 2, -1, 3], np.int32)
+    got, sc, ws = _csr_call(mf, h, to_dev(e), off, ids)
+    assert got.tolist() == [INVALID, INVALID, INVALID, 3]
+    assert np.isnan(sc[:3]).all() and sc[3] == 0.0
+    assert int(ws.sum()) == 0
+
+
+def test_rejects_invalid_metadata(mf):
+    """tests/cuda/cuda_tests.cu:1283-1339 (host checks before any launch)."""
+    import torch
+
+    E = mf.ErrorCode
+    rows, hs, v, mx = 1, 4, 8, 2
+    hidden = torch.zeros(rows * hs, dtype=torch.float16, device="cuda")
+    emb = torch.zeros(v * hs, dtype=torch.float16, device="cuda")
+    allowed = torch.zeros(rows * mx, dtype=torch.int32, device="cuda")
+    counts = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    out = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    s = _stream()
+    f = mf.restricted_output_head_f16
+    assert f(hidden, emb, allowed, counts, out, 0, hs, v, mx, s).code == E.invalid_argument
+    assert f(hidden, emb, allowed, counts, out, rows, hs, v, 0, s).code == E.invalid_argument
+    assert f(hidden, emb, allowed, counts, out, rows, hs, v, mx, None).code == E.invalid_argument
+    assert f(hidden, emb, allowed, counts, counts, rows, hs, v, mx, s).code == E.invalid_argument
+    assert f(hidden, emb, allowed, counts, out, 2**64 - 1, hs, v, mx, s).code == E.resource_limit
+    assert f(hidden, emb, allowed, counts, out, rows, hs, v, mx, s).ok()
+
+
+def test_greedy_select_kat(mf, golden_dir):
+    """tests/cuda/cuda_tests.cu:508-565 at V = 17 and V = 49,152."""
+    import torch
+    import sys
+
+    sys.path.insert(0, golden_dir)
+    from make_golden import greedy_case
+
+    k = json.load(open(os.path.join(golden_dir, "kat_greedy.json")))
+    for case in k["cases"]:
+        logits, exp = greedy_case(case["rows"], case["vocabulary_size"])
+        assert exp == case["expected"]
+        out = torch.empty(case["rows"], dtype=torch.int32, device="cuda")
+        st = mf.greedy_select_f16(to_dev(logits), out, case["rows"], case["vocabulary_size"], _stream())
+        assert st.ok()
+        assert _u32(out).tolist() == exp
+
+
+def test_greedy_select_rejects(mf):
+    """tests/cuda/cuda_tests.cu:1137-1171."""
+    import torch
+
+    E = mf.ErrorCode
+    logits = torch.zeros(8, dtype=torch.float16, device="cuda")
+    tokens = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = _stream()
+    assert mf.greedy_select_f16(logits, tokens, 0, 8, s).code == E.invalid_argument
+    assert mf.greedy_select_f16(logits, tokens, 1, 8, None).code == E.invalid_argument
+    assert mf.greedy_select_f16(logits, tokens, 1, 7, s).code == E.invalid_argument
+    assert mf.greedy_select_f16(logits, tokens, 1, 2**32, s).code == E.resource_limit
+
+
+def test_pr4_logits_greedy(mf, O, golden_dir):
+    """Real SmolLM2 logits (tests/fixtures/golden/smollm2-pr4-greedy-f32):
+    expected tokens [198, 198, 504]; margins >= 1.0 survive fp16 rounding."""
+    import torch
+
+    z = np.load(os.path.join(golden_dir, "pr4_logits.npz"))
+    lg = z["logits"].astype(np.float16)
+    out = torch.empty(3, dtype=torch.int32, device="cuda")
+    assert mf.greedy_select_f16(to_dev(lg), out, 3, lg.shape[1], _stream()).ok()
+    assert _u32(out).tolist() == z["tokens"].tolist() == O.greedy_select_f16(lg).tolist()
+
+
+def test_restricted_greedy_market_dfa(mf, O, golden_dir):
+    """tests/cuda/cuda_tests.cu:567-697: real market-DFA states; the
+    disallowed logit 100 must lose, an all-NaN row falls back to its lowest id."""
+    import torch
+    import sys
+
+    sys.path.insert(0, golden_dir)
+    from make_golden import market_dfa_case
+
+    z = np.load(os.path.join(golden_dir, "market_dfa.npz"))
+    logits, allowed, counts, expected = market_dfa_case(z["state_offsets"], z["arc_tokens"])
+    assert np.array_equal(expected, z["select_expected"])
+    rows, mx = allowed.shape
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    st = mf.restricted_greedy_select_f16(to_dev(logits), to_dev(allowed), to_dev(counts), out, rows,
+                                         logits.shape[1], mx, _stream())
+    assert st.ok()
+    got = _u32(out)
+    assert np.array_equal(got, expected)
+    assert np.array_equal(got, O.restricted_greedy_select_f16(logits, allowed, counts, mx))
+
+
+def test_restricted_greedy_invalid_rows(mf):
+    """tests/cuda/cuda_tests.cu:1173-1277."""
+    import torch
+
+    E = mf.ErrorCode
+    logits = torch.zeros(8, dtype=torch.float16, device="cuda")
+    allowed = to_dev(np.array([1, 3, 5, 7], np.uint32))
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    s = _stream()
+    for counts, al in (([0], [1, 3, 5, 7]), ([5], [1, 3, 5, 7]), ([2], [1, 8, 5, 7])):
+        st = mf.restricted_greedy_select_f16(logits, to_dev(np.array(al, np.uint32)),
+                                             to_dev(np.array(counts, np.uint32)), out, 1, 8, 4, s)
+        assert st.ok()
+        assert _u32(out)[0] == INVALID
+    counts = to_dev(np.array([2], np.uint32))
+    f = mf.restricted_greedy_select_f16
+    assert f(logits, allowed, counts, out, 1, 8, 0, s).code == E.invalid_argument
+    assert f(logits, allowed, counts, out, 1, 8, 3, s).code == E.invalid_argument
+    assert f(logits, allowed, counts, counts, 1, 8, 4, s).code == E.invalid_argument
+
+
+# ---- seeded parity against the CPU oracle ---------------------------------
+
+def _ragged_case(seed, rows, kmax, sort_ids=False):
+    from market_sim_b200 import synth
+
+    h = synth.hidden_states(seed, rows)
+    off, ids = synth.ragged_batch(seed, rows=rows, kmax=kmax, sort_ids=sort_ids)
+    return h, off, ids
+
+
+@pytest.mark.parametrize("rows,kmax,sort_ids", [(1, 1, False), (1, 16, False), (7, 64, True),
+                                                (32, 4096, False), (256, 4096, False),
+                                                (256, 4096, True)])
+def test_csr_parity_vs_oracle(mf, O, emb_full, rows, kmax, sort_ids):
+    e, e_dev = emb_full
+    h, off, ids = _ragged_case(1000 + rows + kmax, rows, kmax, sort_ids)
+    got, sc, ws = _csr_call(mf, h, e_dev, off, ids)
+    oid, obest, oru = O.restricted_head_csr(h, e, off, ids, threads=8)
+    check_head_parity(got, sc, oid, obest, oru)
+    assert int(ws.sum()) == 0
+
+
+def test_csr_long_single_row_full_vocab(mf, O, emb_full):
+    """One row allowing every token (K = 49,152): split over the whole GPU."""
+    from market_sim_b200 import synth
+
+    e, e_dev = emb_full
+    h = synth.hidden_states(5, 1)
+    ids = synth.sample_without_replacement(5, 9, 49_152, 49_152)
+    off = np.array([0, ids.size], np.int32)
+    got, sc, _ = _csr_call(mf, h, e_dev, off, ids)
+    oid, obest, oru = O.restricted_head_csr(h, e, off, ids)
+    check_head_parity(got, sc, oid, obest, oru)
+    dense, dbest, _ = O.dense_head(h, e)
+    assert oid[0] == dense[0]
+
+
+def test_csr_ties_nan_and_mixed(mf, O):
+    """Duplicate embedding rows tie (lowest id wins), NaN hidden rows fall back
+    to the lowest candidate, a NaN embedding row never wins, -0 ties +0."""
+    from market_sim_b200 import synth
+
+    v = 4096
+    e = synth.embedding(77, vocab=v)
+    e[100] = e[3000]
+    e[200] = np.float16(np.nan)
+    e[300] = 0
+    e[301] = -0.0
+    h = synth.hidden_states(78, 5)
+    h[1] = np.float16(np.nan)
+    off = np.array([0, 2, 5, 7, 9, 11], np.int32)
+    # row 0: exact tie 3000 vs 100 (pick 100); row 1: NaN hidden -> lowest (7)
+    # row 2: NaN embedding row 200 with a finite one; row 3: +0 vs -0 rows
+    # (scores +0 and -0 tie -> 300); row 4: a plain pair
+    ids = np.array([3000, 100, 50, 7, 9000 % v, 200, 5, 301, 300, 11, 12], np.int32)
+    got, sc, _ = _csr_call(mf, h, to_dev(e), off, ids)
+    oid, obest, oru = O.restricted_head_csr(h, e, off, ids)
+    assert got[0] == 100 and oid[0] == 100
+    assert got[1] == 7 and oid[1] == 7
+    assert got[2] == 5 and oid[2] == 5
+    assert got[3] == 300 and oid[3] == 300
+    assert got[4] == oid[4]
+
+
+def test_csr_malformed_offsets_gives_sentinel_and_recovers(mf, O, emb_full):
+    import torch
+
+    e, e_dev = emb_full
+    h, off, ids = _ragged_case(4, 16, 256)
+    bad = off.copy()
+    bad[5], bad[6] = bad[6], bad[5]  # decreasing step
+    ws = torch.zeros(mf.head_workspace_bytes(16), dtype=torch.uint8, device="cuda")
+    got, sc, ws = _csr_call(mf, h, e_dev, bad, ids, ws=ws)
+    assert (got == INVALID).all() and np.isnan(sc).all()
+    assert int(ws.sum()) == 0
+    bad2 = off.copy()
+    bad2[-1] -= 1  # last offset does not match the ids size
+    got, _, ws = _csr_call(mf, h, e_dev, bad2, ids, ws=ws)
+    assert (got == INVALID).all() and int(ws.sum()) == 0
+    got, sc, ws = _csr_call(mf, h, e_dev, off, ids, ws=ws)
+    oid, obest, oru = O.restricted_head_csr(h, e, off, ids)
+    check_head_parity(got, sc, oid, obest, oru)
+
+
+def test_csr_deterministic_repeats(mf, emb_full):
+    _, e_dev = emb_full
+    h, off, ids = _ragged_case(9, 128, 4096)
+    first = _csr_call(mf, h, e_dev, off, ids)
+    for _ in range(5):
+        again = _csr_call(mf, h, e_dev, off, ids)
+        assert np.array_equal(first[0], again[0])
+        assert np.array_equal(first[1].view(np.uint32), again[1].view(np.uint32))
+
+
+@pytest.mark.parametrize("rows", [1, 16, 256])
+@pytest.mark.parametrize("k", [2, 8, 32, 128])
+def test_padded_reference_bench_cells(mf, O, emb_full, rows, k):
+    """The reference bench's 12 cells (src/tools/cuda_restricted_output_head_bench.cu:129-140):
+    patterned hidden rows and ids (row*131 + c*977 + 17) % V, padded table."""
+    import torch
+
+    e, e_dev = emb_full
+    v = e.shape[0]
+    h = np.array([0.5 + (i % 13) / 32.0 for i in range(rows * 576)], np.float32).astype(np.float16)
+    allowed = np.array([[(r * 131 + c * 977 + 17) % v for c in range(k)] for r in range(rows)], np.uint32)
+    counts = np.full(rows, k, np.uint32)
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    st = mf.restricted_output_head_f16(to_dev(h), e_dev, to_dev(allowed), to_dev(counts), out, rows,
+                                       576, v, k, _stream())
+    assert st.ok()
+    oid, obest = O.restricted_head_padded(h.reshape(rows, 576), e, allowed, counts, k)
+    off = np.arange(rows + 1, dtype=np.int32) * k
+    _, _, oru = O.restricted_head_csr(h.reshape(rows, 576), e, off, allowed.astype(np.int32).reshape(-1))
+    check_head_parity(_u32(out), None, oid, obest, oru)
+
+
+def test_padded_matches_csr(mf, emb_full):
+    """The padded (reference-signature) path and the ragged path agree."""
+    import torch
+
+    e, e_dev = emb_full
+    h, off, ids = _ragged_case(31, 64, 300)
+    rows = 64
+    counts = np.diff(off).astype(np.uint32)
+    mx = int(counts.max())
+    allowed = np.zeros((rows, mx), np.uint32)
+    for r in range(rows):
+        allowed[r, :counts[r]] = ids[off[r]:off[r + 1]]
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    assert mf.restricted_output_head_f16(to_dev(h), e_dev, to_dev(allowed), to_dev(counts), out, rows,
+                                         576, e.shape[0], mx, _stream()).ok()
+    got, _, _ = _csr_call(mf, h, e_dev, off, ids)
+    assert np.array_equal(_u32(out), got)
