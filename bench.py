@@ -71,6 +71,9 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            t = time.time()
+            while not self.lines and time.time() - t < 5:  # first sample before timing
+                time.sleep(0.02)
         except FileNotFoundError:
             self.proc = None
         return self
@@ -179,26 +182,43 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # (1) headline: the K steps captured once in a CUDA graph (each node one
+    # launch of the head through the C-ABI), replayed in the timed region
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                step(args.warmup + i)
+        graph.replay()  # untimed warm replay
+    stream.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             t0.record(stream)
-            for i in range(args.steps):
-                starts[i].record(stream)
-                step(args.warmup + i)
-                ends[i].record(stream)
+            graph.replay()
             t1.record(stream)
         torch.cuda.synchronize()
     barrier()
     total_ms = max_over_ranks(t0.elapsed_time(t1))
-    kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    avg_kernel_ms = statistics.fmean(kernel_ms)
+    del graph
+
+    # (2) roofline: per-launch CUDA events on the launching stream
+    n_ev = min(args.steps, 2000)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(n_ev):
+            starts[i].record(stream)
+            step(args.warmup + i)
+            ends[i].record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = [s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)]
+    avg_kernel_ms = max_over_ranks(statistics.fmean(kernel_ms))
     alg_bytes = statistics.fmean(batches[(args.warmup + i) % BATCHES]["alg_bytes"]
-                                 for i in range(args.steps))
+                                 for i in range(n_ev))
 
     # end to end through the public API: pinned host inputs -> H2D, launch,
     # D2H of the selected ids and scores, every step
@@ -266,6 +286,9 @@ def run_ours(args):
         "e2e": {"value": ROWS * world * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps},
         "gpu_launches": args.steps,
+        "timing": {"value": "CUDA graph of the K launches, events around one replay",
+                   "roofline": f"per-launch CUDA events over {n_ev} launches",
+                   "e2e": "per-step public-API calls with pinned H2D + D2H, events around K steps"},
         "clocks": clocks.summary(),
     }
     if rank == 0 and not args.no_cpu:
@@ -356,8 +379,8 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

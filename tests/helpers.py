@@ -45,3 +45,21 @@ def check_head_parity(gpu_ids, gpu_scores, orc_ids, orc_best, orc_runner_up):
         loose = finite & ~strict
         np.testing.assert_allclose(gs[loose], best[loose], rtol=SCORE_RTOL, atol=MARGIN)
     return int((finite & (margin < MARGIN)).sum())
+
+
+_STREAM = None
+
+
+def gpu_stream():
+    """A dedicated non-blocking CUDA stream (the reference's CudaStream is
+    created cudaStreamNonBlocking, src/cuda/cuda_stream.cu:13; the legacy
+    default stream has handle 0, which the API rejects as a null stream).
+    Inputs are staged with synchronous copies, and results are read after
+    torch.cuda.synchronize()."""
+    global _STREAM
+    import torch
+
+    if _STREAM is None:
+        _STREAM = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    return _STREAM

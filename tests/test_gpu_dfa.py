@@ -8,7 +8,7 @@ import os
 import numpy as np
 import pytest
 
-from helpers import INVALID, to_dev
+from helpers import INVALID, gpu_stream, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -28,9 +28,7 @@ def O():
 
 
 def _stream():
-    import torch
-
-    return torch.cuda.current_stream()
+    return gpu_stream()
 
 
 def _decode(mf, hidden, e_dev, off, tok, nxt, init, num_states):
@@ -105,6 +103,7 @@ def test_dfa_step_invalid_states(mf, cuda):
     st = mf.dfa_head_step_f16(to_dev(h), to_dev(e), to_dev(off), to_dev(tok), to_dev(nxt), states_in,
                               states_out, out, None, ws, 4, 3, 576, 1024, _stream())
     assert st.ok(), st
+    torch.cuda.synchronize()
     got = out.cpu().numpy().view(np.uint32)
     so = states_out.cpu().numpy()
     assert got[1] == INVALID and so[1] == 1

@@ -11,7 +11,7 @@ import os
 import numpy as np
 import pytest
 
-from helpers import INVALID, check_head_parity, to_dev
+from helpers import INVALID, check_head_parity, gpu_stream, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -39,13 +39,14 @@ def emb_full(cuda):
 
 
 def _u32(t):
+    import torch
+
+    torch.cuda.synchronize()
     return t.cpu().numpy().view(np.uint32)
 
 
 def _stream():
-    import torch
-
-    return torch.cuda.current_stream()
+    return gpu_stream()
 
 
 def _csr_call(mf, hidden, emb_dev, offsets, ids, vocab=None, hidden_size=None, ws=None):
