@@ -170,6 +170,32 @@ MF_API mf_status mf_dfa_decode_f16(const void* hidden, uint64_t hidden_bytes,
                             uint64_t steps, uint64_t batch, uint64_t num_states,
                             uint64_t hidden_size, uint64_t vocab, void* stream);
 
+/* ---- allocation-free ragged head ----------------------------------------
+ *
+ * No counterpart in the reference.  The same ragged CSR head as
+ * mf_head_restricted_csr_f16, for callers that cannot allocate device
+ * memory (code running where cudaMalloc is forbidden or unavailable: inside
+ * a host callback, under an allocator that must not grow, or an embedding
+ * runtime that hands out only its own input/output buffers).  Its scratch is
+ * a fixed array of MF_NOALLOC_SCRATCH_BYTES in this library's device memory,
+ * held by every GPU that loads the library until the process exits; rows is
+ * limited to MF_NOALLOC_MAX_ROWS (larger batches get MF_RESOURCE_LIMIT).
+ * The first call on each device looks the array up (cudaGetSymbolAddress),
+ * so make that first call before any stream capture.  Each call clears the
+ * part of the array it uses (cudaMemsetAsync on `stream`) and calls no
+ * allocator.  All calls on a device share the one array: calls that overlap
+ * on the GPU (different streams, no ordering between them) race and give
+ * wrong results, so serialise them.  Arguments and results are otherwise
+ * those of mf_head_restricted_csr_f16. */
+#define MF_NOALLOC_MAX_ROWS 65536u
+#define MF_NOALLOC_SCRATCH_BYTES (MF_NOALLOC_MAX_ROWS * 12u + 16u)
+
+MF_API mf_status mf_head_restricted_csr_f16_noalloc(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    uint64_t rows, uint64_t hidden_size, uint64_t vocab, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

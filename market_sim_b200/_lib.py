@@ -36,6 +36,9 @@ _SIGNATURES = {
                           _P, _U64, _P, _U64, _U64, _U64, _U64, _U64, _U64, _P],
 }
 
+_SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
+                                                     _U64, _P, _U64, _U64, _U64, _U64, _P]
+
 _U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64]}
 _U32_FUNCS = {"mf_version": [], "mf_built_arch": []}
 

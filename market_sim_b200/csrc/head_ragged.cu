@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <initializer_list>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -616,4 +617,57 @@ extern "C" mf_status mf_dfa_decode_f16(
     if (e != cudaSuccess) return launch_status(e);
   }
   return ok();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of mf_head_restricted_csr_f16 (no counterpart in
+// the reference).  For callers that may not allocate device memory: the
+// workspace is this fixed device array instead of a caller buffer.  Every
+// GPU that loads the library holds it until the process exits.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MF_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name is only a stand-in, never a device pointer, so the
+// address comes from cudaGetSymbolAddress, once per device (cached).
+cudaError_t noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" mf_status mf_head_restricted_csr_f16_noalloc(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    uint64_t rows, uint64_t hidden_size, uint64_t vocab, void* stream) {
+  if (rows == 0 || stream == nullptr) return fail(MF_INVALID_ARGUMENT);
+  if (rows > MF_NOALLOC_MAX_ROWS) return fail(MF_RESOURCE_LIMIT);
+  void* scratch = nullptr;
+  cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+  const uint64_t bytes = mf_head_workspace_bytes(rows);  // <= MF_NOALLOC_SCRATCH_BYTES
+  // the kernel needs its keys, counters and control words at zero
+  e = cudaMemsetAsync(scratch, 0, bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+  return mf_head_restricted_csr_f16(hidden, hidden_bytes, embedding, embedding_bytes, offsets,
+                                    offsets_bytes, ids, ids_bytes, out_ids, out_ids_bytes,
+                                    out_scores, out_scores_bytes, scratch, bytes, rows,
+                                    hidden_size, vocab, stream);
 }

@@ -248,6 +248,23 @@ def restricted_output_head_csr_f16(hidden: Buffer, embedding: Buffer, offsets: B
         *_pb(workspace), rows, hidden_size, vocabulary_size, _sp(stream)))
 
 
+NOALLOC_MAX_ROWS = 65536
+"""Largest batch ``restricted_output_head_csr_f16_noalloc`` accepts."""
+
+
+def restricted_output_head_csr_f16_noalloc(hidden: Buffer, embedding: Buffer, offsets: Buffer,
+                                           ids: Buffer, token_ids: Buffer,
+                                           scores: Optional[Buffer], rows: int, hidden_size: int,
+                                           vocabulary_size: int, stream) -> Status:
+    """The ragged head without a workspace argument, for callers that cannot
+    allocate device memory: the library keeps a fixed scratch array per GPU
+    (up to NOALLOC_MAX_ROWS rows).  Calls sharing a device must not overlap
+    on the GPU; make the first call on a device before any stream capture."""
+    return _status(lib.mf_head_restricted_csr_f16_noalloc(
+        *_pb(hidden), *_pb(embedding), *_pb(offsets), *_pb(ids), *_pb(token_ids), *_pb(scores),
+        rows, hidden_size, vocabulary_size, _sp(stream)))
+
+
 def dfa_head_step_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer,
                       arc_tokens: Buffer, arc_next: Buffer, states_in: Buffer,
                       states_out: Buffer, tokens: Buffer, scores: Optional[Buffer],
