@@ -170,6 +170,39 @@ MF_API mf_status mf_dfa_decode_f16(const void* hidden, uint64_t hidden_bytes,
                             uint64_t steps, uint64_t batch, uint64_t num_states,
                             uint64_t hidden_size, uint64_t vocab, void* stream);
 
+/* ---- dense full-vocabulary head (tcgen05) --------------------------------
+ *
+ * Replaces linear_f16 (cuBLAS logits, include/marketforge/cuda/linear.hpp:18-22,
+ * src/cuda/linear.cu:40-104) followed by greedy_select_f16 (greedy.hpp:17-21):
+ * one kernel computes FP32 scores of every vocabulary row of a shard with
+ * the tensor cores and keeps only each row's best (score, id).  hidden: fp16
+ * [rows, hidden_size]; embedding: fp16 [vocab_rows, hidden_size], the rows
+ * of vocabulary ids [vocab_begin, vocab_begin + vocab_rows).  hidden_size is
+ * a multiple of 64 up to 576; rows <= 128 x SM count.  Outputs (either may
+ * be NULL, not both): out_keys u64 [rows] — the packed key whose unsigned
+ * max over shards is the global selection (so vocabulary shards on several
+ * GPUs merge with one max all-reduce, then mf_decode_keys) — and out_ids u32
+ * [rows] / out_scores f32 [rows] for this shard.  A row whose scores are all
+ * NaN selects vocab_begin (greedy_select_f16's "token 0" rule per shard).
+ * Workspace rule as for mf_head_restricted_csr_f16, sized by
+ * mf_dense_workspace_bytes(rows). */
+MF_API uint64_t mf_dense_workspace_bytes(uint64_t rows);
+
+MF_API mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes,
+                                   const void* embedding, uint64_t embedding_bytes,
+                                   void* out_keys, uint64_t out_keys_bytes,
+                                   void* out_ids, uint64_t out_ids_bytes,
+                                   void* out_scores, uint64_t out_scores_bytes,
+                                   void* workspace, uint64_t workspace_bytes,
+                                   uint64_t rows, uint64_t hidden_size,
+                                   uint64_t vocab_rows, uint64_t vocab_begin, void* stream);
+
+/* Decodes packed keys (e.g. after a max all-reduce across vocabulary shards)
+ * to ids u32 [rows] and, if out_scores is not NULL, FP32 scores. */
+MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out_ids,
+                                uint64_t out_ids_bytes, void* out_scores,
+                                uint64_t out_scores_bytes, uint64_t rows, void* stream);
+
 /* ---- allocation-free ragged head ----------------------------------------
  *
  * No counterpart in the reference.  The same ragged CSR head as

@@ -39,7 +39,12 @@ _SIGNATURES = {
 _SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
                                                      _U64, _P, _U64, _U64, _U64, _U64, _P]
 
-_U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64]}
+_SIGNATURES["mf_dense_head_f16"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
+                                    _U64, _U64, _U64, _U64, _P]
+_SIGNATURES["mf_decode_keys"] = [_P, _U64, _P, _U64, _P, _U64, _U64, _P]
+
+_U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64],
+              "mf_dense_workspace_bytes": [_U64]}
 _U32_FUNCS = {"mf_version": [], "mf_built_arch": []}
 
 # Optional entry points: bound when the library exports them.

@@ -1,0 +1,530 @@
+// Dense (full-vocabulary) head: tcgen05 GEMM with the greedy argmax fused
+// into the TMEM epilogue; logits are never written to memory.
+//
+// Replaces the reference's two-pass full head: linear_f16 (cublasGemmEx into
+// fp16 logits [rows, V], src/cuda/linear.cu:40-104) followed by
+// greedy_select_f16 (src/cuda/greedy.cu:21-59, 237-279).  Here the scores
+// stay FP32 and only one packed (score, id) key per row leaves the SM.
+//
+// Tile = 128 hidden rows (M) x 256 vocabulary rows (N); K = hidden width in
+// 64-element (128-byte) chunks.  One CTA per SM, persistent:
+//   * CTA (m, q) keeps hidden tile m resident in shared memory (loaded once
+//     by TMA, 128-byte swizzle, K-major) and walks vocabulary tiles
+//     n = q, q + Q, q + 2Q, ...  The CTAs that share an n sequence run
+//     together, so each embedding tile comes from DRAM once and from L2 for
+//     the other hidden tiles;
+//   * warp 0 (one lane) streams embedding chunks with TMA into a 2-stage
+//     ring (no multicast: a plain tiled load of this GPU's memory);
+//   * warp 1 owns TMEM (512 columns = two 128 x 256 f32 accumulators) and
+//     one lane issues tcgen05.mma.kind::f16 (4 per chunk), committing to
+//     the ring's "empty" barriers and to the accumulator's "full" barrier;
+//   * warps 2-9 drain the other accumulator with tcgen05.ld while the next
+//     tile accumulates: thread = one hidden row and half of the tile's 256
+//     columns; per 64 columns a NaN-ignoring max tree, and only when it beats
+//     the running best, a search for the lowest column holding it (columns
+//     scanned in increasing id order keep the lowest id on ties; NaN never
+//     wins).
+// At the end each row's key is merged with atomicMax into the workspace; the
+// last CTA out decodes keys to ids/scores and clears the workspace.  The key
+// order is the selection rule (see common.cuh), so vocabulary shards on
+// several GPUs merge with a plain max-reduction of the keys.
+//
+// Every mbarrier wait is bounded; a wait that runs out sets an abort flag
+// and the error word in the workspace, and the CTA drains its in-flight
+// copies and MMAs (bounded again) before freeing TMEM and exiting.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <initializer_list>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace mfb {
+namespace dense {
+
+constexpr int kBM = 128;          // hidden rows per tile (MMA M)
+constexpr int kBN = 256;          // vocabulary rows per tile (MMA N)
+constexpr int kBK = 64;           // K elements per chunk (one 128-byte swizzle atom)
+constexpr int kMaxKChunks = 9;    // hidden width up to 576
+constexpr int kStages = 2;        // embedding chunks in flight
+constexpr int kAChunkBytes = kBM * kBK * 2;  // 16 KB
+constexpr int kBChunkBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kEpiWarps = 8;      // two per TMEM lane quadrant, each on half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA, epilogue warps
+constexpr uint32_t kTmemCols = 512;
+constexpr uint64_t kWaitLimitNs = 100ull * 1000 * 1000;  // 100 ms per mbarrier wait
+
+struct Smem {  // offsets inside the 1024-aligned dynamic shared memory
+  static constexpr int a = 0;
+  static constexpr int b = kMaxKChunks * kAChunkBytes;             // 147,456
+  static constexpr int bars = b + kStages * kBChunkBytes;          // 212,992
+  // barriers: a_full, b_full[2], b_empty[2], acc_full[2], acc_empty[2], drain
+  static constexpr int n_bars = 10;
+  static constexpr int tmem_slot = bars + n_bars * 8;
+  static constexpr int abort_flag = tmem_slot + 4;
+  static constexpr int issued = abort_flag + 4;  // u32[kStages]: TMA loads issued per stage
+  static constexpr int size = issued + 4 * kStages;
+};
+constexpr size_t kSmemBytes = Smem::size + 1024;  // + alignment slack
+
+struct Params {
+  uint32_t rows;        // hidden rows (batch)
+  uint32_t k_chunks;    // hidden width / 64
+  uint32_t vocab_rows;  // rows of this vocabulary shard
+  uint32_t vocab_begin; // global id of shard row 0
+  uint32_t m_tiles, n_tiles, per_m;
+  unsigned long long* keys;  // workspace: rows keys
+  uint32_t* control;         // workspace: done counter, error word
+  unsigned long long* out_keys;
+  uint32_t* out_ids;
+  float* out_scores;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase of parity `parity` of `bar`, for at most kWaitLimitNs.
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t start = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 255u) == 255u && global_ns() - start > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(16u >> 4) << 16;    // leading byte offset (unused for this layout)
+  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset
+  d |= 1ull << 46;                    // descriptor version
+  d |= 2ull << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16: F32 accumulator, F16 A and B, both
+// K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 TMEM lanes x 64 consecutive f32 columns -> 64 registers per thread.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
+                  const __grid_constant__ CUtensorMap tm_emb, Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(sm);
+  const uint32_t bar0 = sbase + Smem::bars;
+  const uint32_t a_full = bar0;
+  auto b_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto b_empty = [&](int s) { return bar0 + 8 * (3 + s); };
+  auto acc_full = [&](int b) { return bar0 + 8 * (5 + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8 * (7 + b); };
+  const uint32_t drain = bar0 + 8 * 9;
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(sm + Smem::abort_flag);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Smem::tmem_slot);
+  volatile uint32_t* issued = reinterpret_cast<volatile uint32_t*>(sm + Smem::issued);
+  __shared__ uint32_t s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t m = blockIdx.x % p.m_tiles;  // hidden tile
+  const uint32_t q = blockIdx.x / p.m_tiles;  // position in the vocabulary walk
+  const uint32_t my_tiles = q < p.n_tiles ? (p.n_tiles - q + p.per_m - 1) / p.per_m : 0;
+
+  if (threadIdx.x == 0) {
+    bar_init(a_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      bar_init(b_full(s), 1);
+      bar_init(b_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(acc_full(b), 1);
+      bar_init(acc_empty(b), kEpiWarps);  // one arrival per epilogue warp
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0u;
+    for (int s = 0; s < kStages; ++s) issued[s] = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // TMEM: 512 columns, two 256-column accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t chunks = p.k_chunks;
+
+  if (warp == 0) {
+    // ---- producer: hidden tile once, then the embedding chunks ----
+    if (lane == 0 && my_tiles > 0) {
+      bar_expect_tx(a_full, chunks * kAChunkBytes);
+      for (uint32_t kc = 0; kc < chunks; ++kc)
+        tma_load_2d(sbase + Smem::a + kc * kAChunkBytes, &tm_hidden, (int)(kc * kBK),
+                    (int)(m * kBM), a_full);
+      uint32_t it = 0;
+      for (uint32_t t = 0; t < my_tiles && !*abort_flag; ++t) {
+        const uint32_t n = q + t * p.per_m;
+        for (uint32_t kc = 0; kc < chunks; ++kc, ++it) {
+          const int s = (int)(it % kStages);
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!bar_wait(b_empty(s), ph ^ 1u)) {
+            *abort_flag = 1u;
+            break;
+          }
+          bar_expect_tx(b_full(s), kBChunkBytes);
+          tma_load_2d(sbase + Smem::b + s * kBChunkBytes, &tm_emb, (int)(kc * kBK),
+                      (int)(n * kBN), b_full(s));
+          issued[s] = issued[s] + 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0 && my_tiles > 0) {
+      bool ok = bar_wait(a_full, 0);
+      uint32_t it = 0;
+      for (uint32_t t = 0; ok && t < my_tiles && !*abort_flag; ++t) {
+        const uint32_t buf = t & 1u;
+        if (!bar_wait(acc_empty(buf), ((t >> 1) & 1u) ^ 1u)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t d = tmem + buf * kBN;
+        for (uint32_t kc = 0; kc < chunks; ++kc, ++it) {
+          const int s = (int)(it % kStages);
+          if (!bar_wait(b_full(s), (it / kStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t a_addr = sbase + Smem::a + kc * kAChunkBytes;
+          const uint32_t b_addr = sbase + Smem::b + s * kBChunkBytes;
+#pragma unroll
+          for (int k4 = 0; k4 < kBK / 16; ++k4)  // 16-element K steps inside the atom
+            mma_f16(d, sw128_desc(a_addr + 32 * k4), sw128_desc(b_addr + 32 * k4),
+                    (kc | (uint32_t)k4) != 0u);
+          mma_commit(b_empty(s));  // frees the stage once these MMAs have read it
+        }
+        if (!ok) break;
+        mma_commit(acc_full(buf));
+      }
+      if (!ok) *abort_flag = 1u;
+      // all MMAs issued so far complete before TMEM is released
+      mma_commit(drain);
+      bar_wait(drain, 0);
+    }
+  } else {
+    // ---- epilogue: warps 2-9; warp w serves TMEM lanes 32 (w % 4) .. +31
+    // (one hidden row per thread) and column half (w - 2) / 4 of each tile ----
+    const uint32_t quad = (uint32_t)(warp & 3);
+    const uint32_t half = (uint32_t)(warp - 2) >> 2;
+    const uint32_t row = m * kBM + quad * 32 + (uint32_t)lane;
+    const float qnan = __uint_as_float(0x7FC00000u);
+    float best = __uint_as_float(0xFF800000u);  // -inf
+    uint32_t best_col = 0xFFFFFFFFu;
+    for (uint32_t t = 0; t < my_tiles; ++t) {
+      const uint32_t buf = t & 1u;
+      if (*abort_flag || !bar_wait(acc_full(buf), (t >> 1) & 1u)) {
+        *abort_flag = 1u;
+        break;
+      }
+      fence_after();
+      const uint32_t n = q + t * p.per_m;
+#pragma unroll 1
+      for (uint32_t c = 0; c < kBN / 2; c += 64) {
+        const uint32_t col0 = n * kBN + half * (kBN / 2) + c;
+        uint32_t r[64];
+        tmem_ld64(tmem + ((quad * 32u) << 16) + buf * kBN + half * (kBN / 2) + c, r);
+        if (col0 + 64 > p.vocab_rows) {  // partial last tile: columns past the shard never win
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (col0 + j >= p.vocab_rows) r[j] = __float_as_uint(qnan);
+        }
+        // fmaxf ignores NaN, so mx is the chunk's best real score (NaN only
+        // if every score is NaN)
+        float mx = __uint_as_float(r[0]);
+#pragma unroll
+        for (int j = 1; j < 64; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+        if (mx > best || (best_col == 0xFFFFFFFFu && mx == mx)) {
+          int first = 0;  // lowest column holding mx
+#pragma unroll
+          for (int j = 63; j >= 0; --j) first = __uint_as_float(r[j]) == mx ? j : first;
+          best = mx;
+          best_col = col0 + (uint32_t)first;
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(acc_empty(buf));
+    }
+    if (my_tiles > 0 && row < p.rows && !*abort_flag) {
+      // all-NaN (or empty) rows: NaN key of the shard's first id, which the
+      // key order ranks below every real score and lowest-id first
+      const unsigned long long key =
+          best_col != 0xFFFFFFFFu ? make_key(best, p.vocab_begin + best_col)
+                                  : make_key(qnan, p.vocab_begin);
+      atomicMax(p.keys + row, key);
+    }
+  }
+
+  // ---- teardown: drain the producer's copies, free TMEM ----
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    // wait (bounded) for the last copy issued into each stage, and the hidden tile
+    atomicOr(p.control + 1, 1u);
+    for (int s = 0; s < kStages; ++s)
+      if (issued[s] > 0u) bar_wait(b_full(s), (issued[s] - 1u) & 1u);
+    if (my_tiles > 0) bar_wait(a_full, 0);
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+
+  // ---- last CTA out: decode the merged keys, clear the workspace ----
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(p.control, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    const bool failed = atomicAdd(p.control + 1, 0u) != 0u;
+    for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+      const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
+      if (failed) p.keys[r] = 0ull;
+      if (p.out_keys) p.out_keys[r] = key;
+      if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
+      if (p.out_scores)
+        p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      p.control[1] = 0u;
+      p.control[0] = 0u;
+    }
+  }
+}
+
+// Decodes merged keys (after a cross-GPU max-reduction) to ids and scores.
+__global__ void decode_keys_kernel(const unsigned long long* keys, uint32_t rows, uint32_t* ids,
+                                   float* scores) {
+  const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const unsigned long long key = keys[r];
+  if (ids) ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
+  if (scores) scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+}
+
+}  // namespace dense
+}  // namespace mfb
+
+using namespace mfb;
+using namespace mfb::dense;
+
+namespace {
+
+mf_status d_ok() { return mf_status{MF_OK, 0}; }
+mf_status d_fail(int32_t code, uint32_t detail = 0) { return mf_status{code, detail}; }
+
+bool d_distinct(std::initializer_list<const void*> ptrs) {
+  const void* seen[16];
+  int n = 0;
+  for (const void* q : ptrs) {
+    if (q == nullptr) continue;
+    for (int i = 0; i < n; ++i)
+      if (seen[i] == q) return false;
+    seen[n++] = q;
+  }
+  return true;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D tensor map over fp16 [rows, width] with (64 x box_rows) boxes, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t width,
+              uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {width, rows};
+  const cuuint64_t strides[1] = {width * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" uint64_t mf_dense_workspace_bytes(uint64_t rows) { return ((rows * 8 + 16) + 15) & ~15ull; }
+
+extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes,
+                                       const void* embedding, uint64_t embedding_bytes,
+                                       void* out_keys, uint64_t out_keys_bytes, void* out_ids,
+                                       uint64_t out_ids_bytes, void* out_scores,
+                                       uint64_t out_scores_bytes, void* workspace,
+                                       uint64_t workspace_bytes, uint64_t rows,
+                                       uint64_t hidden_size, uint64_t vocab_rows,
+                                       uint64_t vocab_begin, void* stream) {
+  if (rows == 0 || hidden_size == 0 || vocab_rows == 0 || stream == nullptr)
+    return d_fail(MF_INVALID_ARGUMENT);
+  if (hidden_size % kBK != 0 || hidden_size > (uint64_t)kMaxKChunks * kBK)
+    return d_fail(MF_RESOURCE_LIMIT);  // widths 64..576 in steps of 64
+  if (vocab_rows > UINT32_MAX || vocab_begin + vocab_rows > UINT32_MAX ||
+      rows > (uint64_t)INT32_MAX)
+    return d_fail(MF_RESOURCE_LIMIT);
+  if (hidden_bytes != rows * hidden_size * 2 || embedding_bytes != vocab_rows * hidden_size * 2 ||
+      (out_keys && out_keys_bytes != rows * 8) || (out_ids && out_ids_bytes != rows * 4) ||
+      (out_scores && out_scores_bytes != rows * 4) ||
+      workspace_bytes < mf_dense_workspace_bytes(rows) || hidden == nullptr ||
+      embedding == nullptr || workspace == nullptr ||
+      (out_keys == nullptr && out_ids == nullptr) ||
+      !d_distinct({hidden, embedding, out_keys, out_ids, out_scores, workspace}) ||
+      (uintptr_t)hidden % 16 != 0 || (uintptr_t)embedding % 16 != 0)
+    return d_fail(MF_INVALID_ARGUMENT);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+  Params p{};
+  p.rows = (uint32_t)rows;
+  p.k_chunks = (uint32_t)(hidden_size / kBK);
+  p.vocab_rows = (uint32_t)vocab_rows;
+  p.vocab_begin = (uint32_t)vocab_begin;
+  p.m_tiles = (uint32_t)((rows + kBM - 1) / kBM);
+  p.n_tiles = (uint32_t)((vocab_rows + kBN - 1) / kBN);
+  if (p.m_tiles > (uint32_t)sms) return d_fail(MF_RESOURCE_LIMIT);  // rows <= 128 x SMs
+  p.per_m = (uint32_t)sms / p.m_tiles;
+  if (p.per_m > p.n_tiles) p.per_m = p.n_tiles;
+  char* ws = static_cast<char*>(workspace);
+  p.keys = reinterpret_cast<unsigned long long*>(ws);
+  p.control = reinterpret_cast<uint32_t*>(ws + rows * 8);
+  p.out_keys = static_cast<unsigned long long*>(out_keys);
+  p.out_ids = static_cast<uint32_t*>(out_ids);
+  p.out_scores = static_cast<float*>(out_scores);
+  CUtensorMap tm_h, tm_e;
+  if (!make_map(&tm_h, hidden, rows, hidden_size, kBM) ||
+      !make_map(&tm_e, embedding, vocab_rows, hidden_size, kBN))
+    return d_fail(MF_CUDA_RUNTIME_FAILURE);
+  static bool attr_set[64] = {};
+  if (!attr_set[dev & 63]) {
+    e = cudaFuncSetAttribute(dense_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBytes);
+    if (e != cudaSuccess) return d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+    attr_set[dev & 63] = true;
+  }
+  const unsigned grid = p.m_tiles * p.per_m;
+  dense_head_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tm_h, tm_e,
+                                                                                      p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_BACKEND_FAILURE, (uint32_t)e);
+}
+
+extern "C" mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out_ids,
+                                    uint64_t out_ids_bytes, void* out_scores,
+                                    uint64_t out_scores_bytes, uint64_t rows, void* stream) {
+  if (rows == 0 || stream == nullptr || keys == nullptr || out_ids == nullptr)
+    return d_fail(MF_INVALID_ARGUMENT);
+  if (rows > (uint64_t)INT32_MAX) return d_fail(MF_RESOURCE_LIMIT);
+  if (keys_bytes != rows * 8 || out_ids_bytes != rows * 4 ||
+      (out_scores && out_scores_bytes != rows * 4) || !d_distinct({keys, out_ids, out_scores}))
+    return d_fail(MF_INVALID_ARGUMENT);
+  decode_keys_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const unsigned long long*>(keys), (uint32_t)rows, static_cast<uint32_t*>(out_ids),
+      static_cast<float*>(out_scores));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_BACKEND_FAILURE, (uint32_t)e);
+}

@@ -288,6 +288,35 @@ def dfa_decode_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer, arc
         num_states, hidden_size, vocabulary_size, _sp(stream)))
 
 
+# ---- dense full-vocabulary head (tcgen05) ---------------------------------
+
+def dense_workspace_bytes(rows: int) -> int:
+    return int(lib.mf_dense_workspace_bytes(rows))
+
+
+def dense_head_f16(hidden: Buffer, embedding: Buffer, keys: Optional[Buffer],
+                   token_ids: Optional[Buffer], scores: Optional[Buffer], workspace: Buffer,
+                   rows: int, hidden_size: int, vocab_rows: int, vocab_begin: int,
+                   stream) -> Status:
+    """Full-vocabulary greedy head over one vocabulary shard (replaces
+    linear_f16 + greedy_select_f16): packed keys and/or ids and scores."""
+    return _status(lib.mf_dense_head_f16(
+        *_pb(hidden), *_pb(embedding), *_pb(keys), *_pb(token_ids), *_pb(scores),
+        *_pb(workspace), rows, hidden_size, vocab_rows, vocab_begin, _sp(stream)))
+
+
+def decode_keys(keys: Buffer, token_ids: Buffer, scores: Optional[Buffer], rows: int,
+                stream) -> Status:
+    """Packed keys (after a cross-shard max) -> ids and scores."""
+    return _status(lib.mf_decode_keys(*_pb(keys), *_pb(token_ids), *_pb(scores), rows,
+                                      _sp(stream)))
+
+
+KEY_SIGN_FLIP = 1 << 63
+"""XOR with this maps the unsigned key order onto signed int64 order, so a
+signed MAX all-reduce (NCCL / torch.distributed) merges keys correctly."""
+
+
 class RaggedHead:
     """Owns the workspace for repeated ragged-head calls on one stream.
 
