@@ -291,12 +291,147 @@ def run_ours(args):
                    "e2e": "per-step public-API calls with pinned H2D + D2H, events around K steps"},
         "clocks": clocks.summary(),
     }
+    if not args.no_secondary:
+        line["secondary"] = {
+            "dense_full_vocab": bench_dense(emb, replicas, device, world, rank, stream,
+                                            barrier, max_over_ranks),
+            "dfa_decode": bench_decode(emb, replicas[0], device, rank, stream, max_over_ranks),
+        }
     if rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(batches[0], emb, budget_s=args.cpu_seconds)
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+DENSE_ROWS = 1024
+DENSE_STEPS = 200
+
+
+def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ranks):
+    """Config 4: B = 1024 RMSNorm'd hidden rows x the full 49,152-row vocabulary,
+    FP32 accumulate, fused argmax.  Under torchrun the vocabulary is sharded
+    (49,152 / N rows per GPU, the tcgen05 kernel over each shard) and the
+    packed keys merge with one NCCL max all-reduce of B x 8 bytes."""
+    import torch
+    import torch.distributed as dist
+
+    from market_sim_b200 import head, synth
+
+    vocab = emb.shape[0]
+    per = vocab // world
+    v0 = rank * per
+    shards = [r[v0:v0 + per] for r in replicas[:3]]  # 3 rotating copies
+    hid = torch.from_numpy(synth.hidden_states(4040, DENSE_ROWS)).to(device)
+    keys = torch.empty(DENSE_ROWS, dtype=torch.int64, device=device)
+    ids = torch.empty(DENSE_ROWS, dtype=torch.int32, device=device)
+    ws = torch.zeros(head.dense_workspace_bytes(DENSE_ROWS), dtype=torch.uint8, device=device)
+    flip = head.KEY_SIGN_FLIP - 2**64
+    h = stream.cuda_stream
+
+    def step(i):
+        st = head.dense_head_f16(hid, shards[i % len(shards)], keys, None, None, ws, DENSE_ROWS,
+                                 576, per, v0, h)
+        if not st.ok():
+            raise RuntimeError(f"dense head failed: {st}")
+        if world > 1:
+            keys.bitwise_xor_(flip)
+            dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+            keys.bitwise_xor_(flip)
+        st = head.decode_keys(keys, ids, None, DENSE_ROWS, h)
+        if not st.ok():
+            raise RuntimeError(f"decode failed: {st}")
+
+    with torch.cuda.stream(stream):
+        for i in range(5):
+            step(i)
+    stream.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(DENSE_STEPS):
+            step(i)
+        t1.record(stream)
+        # the GEMM kernel alone, for the tensor-core roofline
+        k0.record(stream)
+        for i in range(DENSE_STEPS):
+            head.dense_head_f16(hid, shards[i % len(shards)], keys, None, None, ws, DENSE_ROWS, 576,
+                                per, v0, h)
+        k1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / DENSE_STEPS
+    kms = max_over_ranks(k0.elapsed_time(k1)) / DENSE_STEPS
+    flop = 2.0 * DENSE_ROWS * vocab * 576
+    peak = _tensor_peak()
+    per_gpu_tflops = 2.0 * DENSE_ROWS * per * 576 / (kms * 1e-3) / 1e12
+    return {"workload": f"B={DENSE_ROWS} x V={vocab} x 576 fp16, f32 accumulate, fused argmax, "
+                        f"vocab-sharded {per} rows/GPU" + (", NCCL max all-reduce of keys" if world > 1 else ""),
+            "seq_per_s": DENSE_ROWS / (ms * 1e-3), "ms_per_step": ms,
+            "tflops_job": flop / (ms * 1e-3) / 1e12,
+            "kernel_us": kms * 1e3,
+            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peak[0],
+                         "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1]},
+            "steps": DENSE_STEPS}
+
+
+def _tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured (bf16 burst; fp16 runs at the same rate)"
+    return 1590.0, "fallback"
+
+
+def bench_decode(emb, e_dev, device, rank, stream, max_over_ranks, steps=128, batch=64):
+    """Config 5: 64-state synthetic DFA, B = 64 sequences x 128 steps of
+    allowed-set lookup + restricted head + advance, all on the device, the
+    128 steps captured once in a CUDA graph (no host synchronisation)."""
+    import torch
+
+    from market_sim_b200 import head, synth
+
+    off, tok, nxt = synth.synthetic_dfa(4242, num_states=64, kmax=2048)
+    hid = torch.from_numpy(synth.decode_hidden(4242 + rank, steps, batch)).to(device)
+    off_d = torch.from_numpy(off).to(device)
+    tok_d = torch.from_numpy(tok).to(device)
+    nxt_d = torch.from_numpy(nxt.astype(np.int32)).to(device)
+    trace = torch.zeros((steps + 1, batch), dtype=torch.int32, device=device)
+    trace[0] = torch.arange(batch, dtype=torch.int32, device=device) % 64
+    tokens = torch.empty((steps, batch), dtype=torch.int32, device=device)
+    ws = torch.zeros(head.dfa_workspace_bytes(batch), dtype=torch.uint8, device=device)
+    h = stream.cuda_stream
+
+    def run():
+        st = head.dfa_decode_f16(hid, e_dev, off_d, tok_d, nxt_d, trace, tokens, None, ws, steps,
+                                 batch, 64, 576, emb.shape[0], h)
+        if not st.ok():
+            raise RuntimeError(f"decode failed: {st}")
+
+    with torch.cuda.stream(stream):
+        run()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            run()
+        graph.replay()
+    stream.synchronize()
+    reps = 20
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        t1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / reps
+    cand = float(np.diff(off).mean())
+    return {"workload": f"64-state DFA, B={batch}, {steps} steps in one CUDA graph",
+            "ms_per_decode": ms, "us_per_step": ms * 1e3 / steps,
+            "tokens_per_s": batch * steps / (ms * 1e-3),
+            "mean_allowed_set": cand}
 
 
 def cpu_baseline(batch, emb, budget_s=8.0, threads=None):
@@ -383,6 +518,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the dense full-vocab and DFA-decode measurements")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     args = ap.parse_args()
     if args.warmup < 3:

@@ -238,6 +238,10 @@ def head_workspace_bytes(rows: int) -> int:
     return int(lib.mf_head_workspace_bytes(rows))
 
 
+def dfa_workspace_bytes(batch: int) -> int:
+    return int(lib.mf_dfa_workspace_bytes(batch))
+
+
 def restricted_output_head_csr_f16(hidden: Buffer, embedding: Buffer, offsets: Buffer,
                                    ids: Buffer, token_ids: Buffer, scores: Optional[Buffer],
                                    workspace: Buffer, rows: int, hidden_size: int,
