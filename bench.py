@@ -41,6 +41,10 @@ KMAX = 4096
 REPLICAS = 6
 BATCHES = 8
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one launch, from one ncu capture of the same
+# workload (profiles/ragged_head_b256_k4096.md, profiles/dense_head_b1024_v49152.md)
+TRAFFIC_RAGGED = 52.82e6
+TRAFFIC_DENSE = 58.02e6
 
 
 def _peaks():
@@ -282,7 +286,10 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": alg_bytes,
-                     "avg_launch_us": avg_kernel_ms * 1e3, "traffic": None},
+                     "avg_launch_us": avg_kernel_ms * 1e3, "traffic": TRAFFIC_RAGGED,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
+                                       "launch (profiles/ragged_head_b256_k4096.md); below the "
+                                       "algorithmic bytes because repeated rows hit in L2"},
         "e2e": {"value": ROWS * world * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps},
         "gpu_launches": args.steps,
@@ -375,7 +382,8 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
             "tflops_job": flop / (ms * 1e-3) / 1e12,
             "kernel_us": kms * 1e3,
             "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peak[0],
-                         "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1]},
+                         "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1],
+                         "traffic": TRAFFIC_DENSE if world == 1 else None},
             "steps": DENSE_STEPS}
 
 

@@ -57,10 +57,11 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     cpp = sorted(glob.glob(os.path.join(CSRC, "marketforge", "*.cpp")))
     cpp_hdr = sorted(glob.glob(os.path.join(INCLUDE, "marketforge", "**", "*.hpp"), recursive=True))
     if cpp and (force or _stale(CXX_LIB, cpp + cpp_hdr + [LIB])):
-        cuda_inc = os.path.join(os.path.dirname(os.path.dirname(_nvcc_path())), "include")
+        cuda_root = os.path.dirname(os.path.dirname(_nvcc_path()))
         _run(["g++", "-std=c++20", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra",
-              "-I", INCLUDE, "-I", cuda_inc, "-o", CXX_LIB, *cpp,
-              "-L", PKG, "-lmfhead", "-Wl,-rpath,$ORIGIN"])
+              "-I", INCLUDE, "-I", os.path.join(cuda_root, "include"), "-o", CXX_LIB, *cpp,
+              "-L", PKG, "-lmfhead", "-L", os.path.join(cuda_root, "lib64"), "-lcudart",
+              "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + os.path.join(cuda_root, "lib64")])
     return LIB
 
 
