@@ -203,6 +203,34 @@ MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out
                                 uint64_t out_ids_bytes, void* out_scores,
                                 uint64_t out_scores_bytes, uint64_t rows, void* stream);
 
+/* ---- host pipeline for the ragged head ----------------------------------
+ *
+ * No counterpart in the reference (the reference copies each decode step's
+ * inputs and synchronises, src/cuda/smollm2.cu:395-501).  A pipeline owns
+ * `depth` device slots and three streams: mf_pipeline_submit copies one batch
+ * (hidden fp16 [rows, hidden_size], CSR offsets int32 [rows + 1], ids int32
+ * [total_ids]) from host memory to the device, runs the ragged head, and
+ * copies ids (u32 [rows]) and scores (f32 [rows], may be NULL) back into the
+ * caller's host buffers, asynchronously; the copy-in of the next batch
+ * overlaps the head of the current one.  Host buffers should be pinned (a
+ * pageable buffer makes its copy synchronous) and must stay untouched until
+ * mf_pipeline_wait(ticket) returns.  The embedding stays resident on the
+ * device.  mf_pipeline_create allocates the slots (device memory) once. */
+typedef struct mf_pipeline mf_pipeline;
+
+MF_API mf_status mf_pipeline_create(mf_pipeline** pipeline, const void* embedding,
+                                    uint64_t embedding_bytes, uint64_t vocab,
+                                    uint64_t hidden_size, uint64_t max_rows, uint64_t max_ids,
+                                    uint32_t depth);
+MF_API mf_status mf_pipeline_submit(mf_pipeline* pipeline, const void* hidden, uint64_t rows,
+                                    const void* offsets, const void* ids, uint64_t total_ids,
+                                    void* out_ids, void* out_scores, uint64_t* ticket);
+MF_API mf_status mf_pipeline_wait(mf_pipeline* pipeline, uint64_t ticket);
+MF_API mf_status mf_pipeline_synchronize(mf_pipeline* pipeline);
+/* The pipeline's streams: 0 = copy-in, 1 = compute, 2 = copy-out. */
+MF_API void* mf_pipeline_stream(mf_pipeline* pipeline, uint32_t which);
+MF_API void mf_pipeline_destroy(mf_pipeline* pipeline);
+
 /* ---- allocation-free ragged head ----------------------------------------
  *
  * No counterpart in the reference.  The same ragged CSR head as

@@ -43,9 +43,17 @@ _SIGNATURES["mf_dense_head_f16"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, 
                                     _U64, _U64, _U64, _U64, _P]
 _SIGNATURES["mf_decode_keys"] = [_P, _U64, _P, _U64, _P, _U64, _U64, _P]
 
+_SIGNATURES["mf_pipeline_create"] = [ctypes.POINTER(_P), _P, _U64, _U64, _U64, _U64, _U64,
+                                     ctypes.c_uint32]
+_SIGNATURES["mf_pipeline_submit"] = [_P, _P, _U64, _P, _P, _U64, _P, _P, ctypes.POINTER(_U64)]
+_SIGNATURES["mf_pipeline_wait"] = [_P, _U64]
+_SIGNATURES["mf_pipeline_synchronize"] = [_P]
+
 _U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64],
               "mf_dense_workspace_bytes": [_U64]}
 _U32_FUNCS = {"mf_version": [], "mf_built_arch": []}
+_PTR_FUNCS = {"mf_pipeline_stream": [_P, ctypes.c_uint32]}
+_VOID_FUNCS = {"mf_pipeline_destroy": [_P]}
 
 # Optional entry points: bound when the library exports them.
 _OPTIONAL: dict[str, list] = {}
@@ -69,6 +77,14 @@ def _load() -> ctypes.CDLL:
         f = getattr(lib, name)
         f.argtypes = args
         f.restype = ctypes.c_uint32
+    for name, args in _PTR_FUNCS.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = ctypes.c_void_p
+    for name, args in _VOID_FUNCS.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = None
     for name, args in _OPTIONAL.items():
         f = getattr(lib, name, None)
         if f is not None:
@@ -80,4 +96,5 @@ def _load() -> ctypes.CDLL:
 lib = _load()
 
 #: every symbol include/mf_head.h declares (checked by the CPU test suite)
-EXPORTED = sorted(list(_SIGNATURES) + list(_U64_FUNCS) + list(_U32_FUNCS))
+EXPORTED = sorted(list(_SIGNATURES) + list(_U64_FUNCS) + list(_U32_FUNCS) + list(_PTR_FUNCS)
+                  + list(_VOID_FUNCS))

@@ -357,3 +357,69 @@ class RaggedHead:
         if not st.ok():
             raise RuntimeError(f"restricted head failed: {st}")
         return out_ids, out_scores
+
+
+class HostPipeline:
+    """Restricted head over batches that live in host memory (native
+    ``mf_pipeline_*``): each ``submit`` copies one batch (hidden rows, CSR
+    offsets, CSR ids) from pinned host memory to the device on a copy stream,
+    runs the ragged head on a compute stream and copies ids and scores back
+    into pinned host memory on a third stream; ``depth`` device slots rotate,
+    so the copy-in of batch i + 1 overlaps the head of batch i.  Host tensors
+    must stay untouched until ``wait(ticket)`` returns.
+    """
+
+    def __init__(self, embedding, max_rows: int, max_ids: int, depth: int = 2, device=None):
+        self.embedding = embedding  # keeps the device table alive
+        self.vocab, self.hidden_size = int(embedding.shape[0]), int(embedding.shape[1])
+        self._p = ctypes.c_void_p()
+        self._ticket = ctypes.c_uint64()
+        self._ticket_ref = ctypes.byref(self._ticket)
+        st = _status(lib.mf_pipeline_create(ctypes.byref(self._p), *_pb(embedding), self.vocab,
+                                            self.hidden_size, int(max_rows), int(max_ids),
+                                            int(depth)))
+        if not st.ok():
+            raise RuntimeError(f"mf_pipeline_create failed: {st}")
+
+    def stream(self, which: int) -> int:
+        """cudaStream_t of the copy-in (0), compute (1) or copy-out (2) stream."""
+        return int(lib.mf_pipeline_stream(self._p, which) or 0)
+
+    def submit(self, hidden, offsets, ids, out_ids, out_scores=None) -> int:
+        """hidden fp16 [rows, H], offsets int32 [rows + 1], ids int32 [total],
+        out_ids int32 [rows], out_scores float32 [rows] or None: pinned host
+        tensors.  Returns the batch's ticket."""
+        return self.submit_ptrs(hidden.data_ptr(), hidden.shape[0], offsets.data_ptr(),
+                                ids.data_ptr(), ids.shape[0], out_ids.data_ptr(),
+                                out_scores.data_ptr() if out_scores is not None else None)
+
+    def submit_ptrs(self, hidden: int, rows: int, offsets: int, ids: int, total_ids: int,
+                    out_ids: int, out_scores) -> int:
+        """``submit`` with raw host addresses (for callers that keep their own
+        pinned buffers)."""
+        s = lib.mf_pipeline_submit(self._p, hidden, rows, offsets, ids or None, total_ids,
+                                   out_ids, out_scores, self._ticket_ref)
+        if s.code:
+            raise RuntimeError(f"mf_pipeline_submit failed: {_status(s)}")
+        return self._ticket.value
+
+    def wait(self, ticket: int) -> None:
+        st = _status(lib.mf_pipeline_wait(self._p, ticket))
+        if not st.ok():
+            raise RuntimeError(f"mf_pipeline_wait failed: {st}")
+
+    def synchronize(self) -> None:
+        st = _status(lib.mf_pipeline_synchronize(self._p))
+        if not st.ok():
+            raise RuntimeError(f"mf_pipeline_synchronize failed: {st}")
+
+    def close(self) -> None:
+        if self._p:
+            lib.mf_pipeline_destroy(self._p)
+            self._p = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -29,7 +29,7 @@ def declared_symbols():
     for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
         if h.endswith(".h"):
             text = open(os.path.join(ROOT, "include", h)).read()
-            names += re.findall(r"^MF_API\s+\w+\s+(mf_\w+)\(", text, flags=re.M)
+            names += re.findall(r"^MF_API\s+[\w\s*]+?\b(mf_\w+)\(", text, flags=re.M)
     return sorted(set(names))
 
 

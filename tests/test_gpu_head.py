@@ -368,3 +368,25 @@ def test_padded_matches_csr(mf, emb_full):
                                          576, e.shape[0], mx, _stream()).ok()
     got, _, _ = _csr_call(mf, h, e_dev, off, ids)
     assert np.array_equal(_u32(out), got)
+
+
+def test_host_pipeline_matches_direct_calls(mf, emb_full):
+    """head.HostPipeline (pinned host in/out, overlapped copies) returns the
+    same ids and scores as direct device calls, batch after batch."""
+    import torch
+
+    e, e_dev = emb_full
+    pipe = mf.HostPipeline(e_dev, 256, 600_000, depth=2)
+    outs = []
+    cases = [_ragged_case(500 + i, 256, 4096) for i in range(5)]
+    for h, off, ids in cases:
+        oi = torch.empty(256, dtype=torch.int32).pin_memory()
+        osc = torch.empty(256, dtype=torch.float32).pin_memory()
+        pipe.submit(torch.from_numpy(h).pin_memory(), torch.from_numpy(off).pin_memory(),
+                    torch.from_numpy(ids).pin_memory(), oi, osc)
+        outs.append((oi, osc))
+    pipe.synchronize()
+    for (h, off, ids), (oi, osc) in zip(cases, outs):
+        got, sc, _ = _csr_call(mf, h, e_dev, off, ids)
+        assert np.array_equal(oi.numpy().view(np.uint32), got)
+        assert np.array_equal(osc.numpy().view(np.uint32), sc.view(np.uint32))
