@@ -75,7 +75,8 @@ struct Rows<RowMode::kCsr> {
 
 template <>
 struct Rows<RowMode::kDfa> {
-  const int32_t* start;  // shared, rows + 1 entries
+  const int32_t* start;     // shared, rows + 1 entries
+  const int32_t* arc_base;  // shared, rows entries: first arc of each row's state
   __device__ __forceinline__ int64_t at(uint32_t r) const { return start[r]; }
 };
 
@@ -106,14 +107,14 @@ __device__ uint32_t find_row(const Rows<M>& rows_tab, uint32_t rows, int64_t c, 
 template <RowMode M>
 __device__ void finalize_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32_t r,
                              unsigned long long key) {
-  if (M == RowMode::kCsr) {
+  if constexpr (M == RowMode::kCsr) {
     const bool ok = key_is_result(key);
     p.out_ids[r] = ok ? key_id(key) : kInvalid;
     if (p.out_scores) p.out_scores[r] = ok ? key_score(key) : __uint_as_float(0x7FC00000u);
   } else {
     const uint32_t st = p.states_in[r];
     if (key_is_result(key)) {
-      const int64_t arc = (int64_t)p.state_offsets[st] + key_id(key);
+      const int64_t arc = (int64_t)rows_tab.arc_base[r] + key_id(key);
       p.out_ids[r] = (uint32_t)p.ids[arc];
       p.states_out[r] = p.arc_next[arc];
       if (p.out_scores) p.out_scores[r] = key_score(key);
@@ -167,7 +168,7 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
 template <RowMode M, bool kFast>
 __global__ void __launch_bounds__(kThreads, 2)
 ragged_head_kernel(RaggedParams p, int64_t chunk) {
-  extern __shared__ int32_t smem_rows[];  // DFA mode: rows + 1 starts
+  extern __shared__ int32_t smem_rows[];  // DFA mode: rows + 1 starts, then rows arc bases
   __shared__ uint32_t s_last;
 
   Rows<M> rows_tab;
@@ -188,8 +189,9 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
       }
     }
     if (blockIdx.x == 0 && threadIdx.x == 0 &&
-        (p.offsets[0] != 0 || (int64_t)p.offsets[p.rows] != p.total))
+        (p.offsets[0] != 0 || (int64_t)p.offsets[p.rows] != p.total)) {
       atomicOr(p.control + 1, 1u);
+    }
   } else {
     // Allowed-set lookup: per-sequence candidate counts from the DFA, and
     // their exclusive prefix sum in shared memory (every block computes the
@@ -197,12 +199,13 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     const uint32_t rows = p.rows;
     for (uint32_t r = threadIdx.x; r < rows; r += kThreads) {
       const uint32_t st = p.states_in[r];
-      int32_t len = 0;
+      int32_t len = 0, base = 0;
       if (st < p.num_states) {
         const int32_t b = p.state_offsets[st], e = p.state_offsets[st + 1];
-        if (b >= 0 && e > b && (int64_t)e <= p.num_arcs) len = e - b;
+        if (b >= 0 && e > b && (int64_t)e <= p.num_arcs) len = e - b, base = b;
       }
       smem_rows[r + 1] = len;
+      smem_rows[rows + 1 + r] = base;
       if (len == 0 && (r % gridDim.x) == blockIdx.x) {
         p.out_ids[r] = kInvalid;
         p.states_out[r] = st;
@@ -233,6 +236,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     }
     __syncthreads();
     rows_tab.start = smem_rows;
+    if constexpr (M == RowMode::kDfa) rows_tab.arc_base = smem_rows + rows + 1;
     total = smem_rows[rows];
     const int64_t groups = (int64_t)gridDim.x * kGroupsPerBlock;
     chunk = (total + groups - 1) / groups;
@@ -253,7 +257,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     const int32_t* cand;  // candidate token ids of the current row, by flat index
     cand = (M == RowMode::kCsr) ? p.ids : nullptr;
     int64_t arc_base = 0;  // DFA: flat index -> arc index offset
-    if (M == RowMode::kDfa) arc_base = (int64_t)p.state_offsets[p.states_in[r]] - row_b;
+    if constexpr (M == RowMode::kDfa) arc_base = (int64_t)rows_tab.arc_base[r] - row_b;
 
     uint4 h[kFastChunksPerLane];
     if (kFast) load_hidden_fast(p.hidden, r, sub, h);
@@ -272,7 +276,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
           row_e = rows_tab.at(r + 1);
         }
         if (c >= row_e || c < row_b) break;  // malformed offsets: stop
-        if (M == RowMode::kDfa) arc_base = (int64_t)p.state_offsets[p.states_in[r]] - row_b;
+        if constexpr (M == RowMode::kDfa) arc_base = (int64_t)rows_tab.arc_base[r] - row_b;
         if (kFast) load_hidden_fast(p.hidden, r, sub, h);
       }
       // up to two candidates of this row per iteration
@@ -326,10 +330,13 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     flush_row<M>(p, rows_tab, r, row_e - row_b, best, seen, sub);
   }
 
-  // Last block out: if the batch was flagged malformed, give every row the
+  // Last block out (CSR mode; DFA offsets are built in-kernel and cannot be
+  // malformed): if the batch was flagged malformed, give every row the
   // sentinel and clear the whole workspace; then reset the control words.
   // Every thread fences first so its atomics and result stores are ordered
-  // before this block's arrival on the done counter.
+  // before this block's arrival on the done counter (one fence at exit costs
+  // less than fencing each store inside the loop).
+  if constexpr (M == RowMode::kDfa) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -382,6 +389,12 @@ static DeviceInfo& device_info() {
     for (auto& m : d.blocks_per_sm)
       for (int& b : m)
         if (b < 1) b = 1;
+    // DFA mode keeps 2 x batch + 1 ints in shared memory (up to ~64 KB)
+    const int dfa_smem = (2 * kMaxDfaBatch + 1) * (int)sizeof(int32_t);
+    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kDfa, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, dfa_smem);
+    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kDfa, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, dfa_smem);
   }
   return d;
 }
@@ -527,8 +540,7 @@ mf_status dfa_validate(const void* hidden, uint64_t hidden_bytes, const void* em
 cudaError_t dfa_launch(RaggedParams p, bool fast, cudaStream_t s) {
   DeviceInfo& d = device_info();
   const int64_t blocks = (int64_t)d.sms * d.blocks_per_sm[1][fast ? 1 : 0];
-  const size_t smem = (p.rows + 1) * sizeof(int32_t);
-  // (kMaxDfaBatch + 1) * 4 bytes stays under the default 48 KB limit
+  const size_t smem = (2 * (size_t)p.rows + 1) * sizeof(int32_t);  // <= 64 KB
   if (fast)
     ragged_head_kernel<RowMode::kDfa, true><<<(unsigned)blocks, kThreads, smem, s>>>(p, 0);
   else
