@@ -203,6 +203,13 @@ MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out
                                 uint64_t out_ids_bytes, void* out_scores,
                                 uint64_t out_scores_bytes, uint64_t rows, void* stream);
 
+/* Self-test of the dense kernel's bounded waits (no counterpart in the
+ * reference): a tiny dense problem whose loads are never issued, so its
+ * mbarrier waits run out after 100 ms; on return *error_word is 1 and
+ * *invalid_rows is 128 when the kernel gave up cleanly.  Synchronises. */
+MF_API mf_status mf_dense_selftest_wait_timeout(void* stream, uint32_t* error_word,
+                                                uint32_t* invalid_rows);
+
 /* ---- host pipeline for the ragged head ----------------------------------
  *
  * No counterpart in the reference (the reference copies each decode step's

@@ -41,6 +41,8 @@ _SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U6
 
 _SIGNATURES["mf_dense_head_f16"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
                                     _U64, _U64, _U64, _U64, _P]
+_SIGNATURES["mf_dense_selftest_wait_timeout"] = [_P, ctypes.POINTER(ctypes.c_uint32),
+                                                 ctypes.POINTER(ctypes.c_uint32)]
 _SIGNATURES["mf_decode_keys"] = [_P, _U64, _P, _U64, _P, _U64, _U64, _P]
 
 _SIGNATURES["mf_pipeline_create"] = [ctypes.POINTER(_P), _P, _U64, _U64, _U64, _U64, _U64,

@@ -64,8 +64,9 @@ struct Smem {  // offsets inside the 1024-aligned dynamic shared memory
   static constexpr int n_bars = 10;
   static constexpr int tmem_slot = bars + n_bars * 8;
   static constexpr int abort_flag = tmem_slot + 4;
-  static constexpr int issued = abort_flag + 4;  // u32[kStages]: TMA loads issued per stage
-  static constexpr int size = issued + 4 * kStages;
+  // u32[kStages + 1]: TMA loads issued per stage, then 1 if the hidden tile was
+  static constexpr int issued = abort_flag + 4;
+  static constexpr int size = issued + 4 * (kStages + 1);
 };
 constexpr size_t kSmemBytes = Smem::size + 1024;  // + alignment slack
 
@@ -80,6 +81,8 @@ struct Params {
   unsigned long long* out_keys;
   uint32_t* out_ids;
   float* out_scores;
+  uint32_t* error_out;       // optional: receives the error word (self-test)
+  uint32_t skip_loads;       // self-test only: the producer issues nothing
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -215,7 +218,7 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
     }
     bar_init(drain, 1);
     *abort_flag = 0u;
-    for (int s = 0; s < kStages; ++s) issued[s] = 0u;
+    for (int s = 0; s <= kStages; ++s) issued[s] = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // TMEM: 512 columns, two 256-column accumulators
@@ -233,7 +236,8 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
 
   if (warp == 0) {
     // ---- producer: hidden tile once, then the embedding chunks ----
-    if (lane == 0 && my_tiles > 0) {
+    if (lane == 0 && my_tiles > 0 && !p.skip_loads) {
+      issued[kStages] = 1u;  // the hidden tile
       bar_expect_tx(a_full, chunks * kAChunkBytes);
       for (uint32_t kc = 0; kc < chunks; ++kc)
         tma_load_2d(sbase + Smem::a + kc * kAChunkBytes, &tm_hidden, (int)(kc * kBK),
@@ -352,7 +356,7 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
     atomicOr(p.control + 1, 1u);
     for (int s = 0; s < kStages; ++s)
       if (issued[s] > 0u) bar_wait(b_full(s), (issued[s] - 1u) & 1u);
-    if (my_tiles > 0) bar_wait(a_full, 0);
+    if (issued[kStages]) bar_wait(a_full, 0);
   }
   fence_before();
   __syncthreads();
@@ -370,6 +374,7 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
   if (s_last) {
     __threadfence();
     const bool failed = atomicAdd(p.control + 1, 0u) != 0u;
+    if (threadIdx.x == 0 && p.error_out) *p.error_out = failed ? 1u : 0u;
     for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
       const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
       if (failed) p.keys[r] = 0ull;
@@ -527,4 +532,68 @@ extern "C" mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void*
       static_cast<float*>(out_scores));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_BACKEND_FAILURE, (uint32_t)e);
+}
+
+// Self-test of the bounded waits (no counterpart in the reference): runs a
+// 128 x 256 x 64 dense problem whose producer issues no loads, so the MMA
+// and epilogue waits run out (100 ms each).  The kernel must return, give
+// every row the sentinel and report the error word; the context stays
+// usable.  Allocates its small buffers with cudaMalloc and synchronises.
+extern "C" mf_status mf_dense_selftest_wait_timeout(void* stream, uint32_t* error_word,
+                                                    uint32_t* invalid_rows) {
+  if (stream == nullptr || error_word == nullptr || invalid_rows == nullptr)
+    return d_fail(MF_INVALID_ARGUMENT);
+  const uint64_t rows = 128, hs = 64, vocab = 256;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void *hid = nullptr, *emb = nullptr, *ws = nullptr, *ids = nullptr, *err = nullptr;
+  cudaError_t e = cudaMalloc(&hid, rows * hs * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&emb, vocab * hs * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&ws, mf_dense_workspace_bytes(rows));
+  if (e == cudaSuccess) e = cudaMalloc(&ids, rows * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&err, 4);
+  if (e == cudaSuccess) e = cudaMemsetAsync(hid, 0, rows * hs * 2, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(emb, 0, vocab * hs * 2, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, mf_dense_workspace_bytes(rows), s);
+  mf_status st = d_ok();
+  int dev = 0, sms = 0;
+  if (e == cudaSuccess) e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  CUtensorMap tm_h, tm_e;
+  if (e == cudaSuccess && (!make_map(&tm_h, hid, rows, hs, kBM) || !make_map(&tm_e, emb, vocab, hs, kBN)))
+    st = d_fail(MF_CUDA_RUNTIME_FAILURE);
+  if (e == cudaSuccess && st.code == MF_OK)
+    e = cudaFuncSetAttribute(dense_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBytes);
+  if (e == cudaSuccess && st.code == MF_OK) {
+    Params p{};
+    p.rows = (uint32_t)rows;
+    p.k_chunks = 1;
+    p.vocab_rows = (uint32_t)vocab;
+    p.m_tiles = 1;
+    p.n_tiles = 1;
+    p.per_m = 1;
+    p.keys = static_cast<unsigned long long*>(ws);
+    p.control = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + rows * 8);
+    p.out_ids = static_cast<uint32_t*>(ids);
+    p.error_out = static_cast<uint32_t*>(err);
+    p.skip_loads = 1u;
+    dense_head_kernel<<<1, kThreads, kSmemBytes, s>>>(tm_h, tm_e, p);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  if (e == cudaSuccess && st.code == MF_OK) {
+    uint32_t host_ids[128];
+    e = cudaMemcpy(host_ids, ids, sizeof(host_ids), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(error_word, err, 4, cudaMemcpyDeviceToHost);
+    uint32_t bad = 0;
+    for (uint32_t id : host_ids) bad += id == kInvalid;
+    *invalid_rows = bad;
+  }
+  cudaFree(hid);
+  cudaFree(emb);
+  cudaFree(ws);
+  cudaFree(ids);
+  cudaFree(err);
+  if (st.code != MF_OK) return st;
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
 }

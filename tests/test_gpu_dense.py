@@ -134,3 +134,30 @@ def test_dense_rejects(mf):
     assert mf.dense_head_f16(h64, e64, None, ids, None, ws, 4, 64, 8, 0, None).code == E.invalid_argument
     assert mf.dense_head_f16(h64, e64, None, ids, None, ws, 4, 64, 8, 0, s).ok()
     assert INVALID == 0xFFFFFFFF
+
+
+def test_dense_bounded_waits_give_up_cleanly(mf):
+    """Failure detection without a GPU fault: the kernel's producer issues no
+    loads (a barrier that nothing completes), its waits run out after 100 ms,
+    every row gets the sentinel, the error word is reported, and the context
+    stays usable for the next call."""
+    import ctypes
+
+    import torch
+
+    from market_sim_b200._lib import lib
+
+    err, bad = ctypes.c_uint32(7), ctypes.c_uint32(0)
+    s = gpu_stream()
+    st = lib.mf_dense_selftest_wait_timeout(ctypes.c_void_p(s.cuda_stream), ctypes.byref(err),
+                                            ctypes.byref(bad))
+    assert st.code == 0, (st.code, st.detail)
+    assert err.value == 1 and bad.value == 128
+    # the context is still healthy: a normal dense call succeeds
+    from market_sim_b200 import synth
+
+    e = synth.embedding(3, vocab=300)
+    h = synth.hidden_states(4, 64)
+    _, ids, _ = _dense(mf, to_dev(h), to_dev(e), 64, 576, 300)
+    assert (ids < 300).all()
+    torch.cuda.synchronize()
