@@ -309,7 +309,11 @@ def run_ours(args):
             "dense_full_vocab": bench_dense(emb, replicas, device, world, rank, stream,
                                             barrier, max_over_ranks),
             "dfa_decode": bench_decode(emb, replicas[0], device, rank, stream, max_over_ranks),
+            "k_sweep_batch1": bench_k_sweep(replicas, device, stream),
         }
+        if args.sweep:
+            line["secondary"]["k_sweep_batch10k"] = bench_k_sweep(
+                replicas[:2], device, stream, rows_per_launch=10_000, states=2, launches=6)
     if rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(batches[0], emb, budget_s=args.cpu_seconds)
     if world > 1:
@@ -391,6 +395,78 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
                          "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1],
                          "traffic": TRAFFIC_DENSE if world == 1 else None},
             "steps": DENSE_STEPS}
+
+
+K_SWEEP = (1, 8, 64, 512, 4096, 49_152)
+
+
+def bench_k_sweep(replicas, device, stream, rows_per_launch=1, states=16, launches=240):
+    """Config 2: allowed-set size K in {1, 8, 64, 512, 4096, 49152}, ids uniform
+    without replacement, sorted and unsorted.  rows_per_launch = 1 measures the
+    batch-1 latency (each launch one hidden state); larger values measure
+    throughput.  `states` distinct (hidden, allowed set) states rotate with the
+    embedding copies; launches back to back in one CUDA graph."""
+    import torch
+
+    from market_sim_b200 import head, synth
+
+    out = {}
+    for k in K_SWEEP:
+        for sort_ids in (False, True):
+            hid, offs, idss = [], [], []
+            for st in range(states):
+                seed = 70_000 + 131 * k + st
+                h = synth.hidden_states(seed, rows_per_launch)
+                if k >= 49_152:  # every row allows the whole vocabulary
+                    base = synth.sample_without_replacement(seed, 5, 49_152, 49_152)
+                    ids = np.tile(np.sort(base) if sort_ids else base, rows_per_launch)
+                else:
+                    ids = np.concatenate([
+                        (np.sort(x) if sort_ids else x) for x in
+                        (synth.sample_without_replacement(seed, 10 + r, k, 49_152)
+                         for r in range(rows_per_launch))])
+                off = (np.arange(rows_per_launch + 1, dtype=np.int64) * k).astype(np.int32)
+                hid.append(torch.from_numpy(h).to(device))
+                offs.append(torch.from_numpy(off).to(device))
+                idss.append(torch.from_numpy(ids.astype(np.int32)).to(device))
+            o_ids = torch.empty(rows_per_launch, dtype=torch.int32, device=device)
+            o_sc = torch.empty(rows_per_launch, dtype=torch.float32, device=device)
+            ws = torch.zeros(head.head_workspace_bytes(rows_per_launch), dtype=torch.uint8,
+                             device=device)
+            hs = stream.cuda_stream
+
+            def launch(i):
+                st = head.restricted_output_head_csr_f16(
+                    hid[i % states], replicas[i % len(replicas)], offs[i % states],
+                    idss[i % states], o_ids, o_sc, ws, rows_per_launch, 576, 49_152, hs)
+                if not st.ok():
+                    raise RuntimeError(f"k-sweep launch failed: {st}")
+
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    launch(i)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(launches):
+                        launch(i)
+                g.replay()
+            stream.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                a.record(stream)
+                g.replay()
+                b.record(stream)
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1e3 / launches
+            alg = rows_per_launch * (k * (1152 + 4) + 1152 + 12) + 4
+            out[f"K={k}{',sorted' if sort_ids else ''}"] = {
+                "us_per_launch": round(us, 3),
+                "states_per_s": rows_per_launch / (us * 1e-6),
+                "alg_GBps": alg / (us * 1e-6) / 1e9}
+            del g
+    return {"workload": f"{rows_per_launch} hidden state(s) per launch, K ids uniform without "
+                        f"replacement, {states} rotating states x {len(replicas)} embedding copies",
+            "results": out}
 
 
 def _tensor_peak():
@@ -532,6 +608,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sweep", action="store_true",
+                    help="also run the 10k-row K sweep (config 2 throughput; slower to set up)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the dense full-vocab and DFA-decode measurements")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

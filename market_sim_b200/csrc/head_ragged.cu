@@ -145,14 +145,47 @@ __device__ float group_dot_generic(const __half* hidden, const __half* emb, uint
   return group8_sum(a, gmask);
 }
 
-// One flushed (row, key, n) triple: merge and finalise when complete.
+// Per-block merge slots: the groups of a block cover one contiguous range of
+// flat candidates, and each group is the first group of the block to touch at
+// most one row that continues into later groups (its last row), so slot g
+// (g = first toucher) holds that row's partial key and candidate count.
+struct BlockSlots {
+  unsigned long long* key;  // shared [kGroupsPerBlock]
+  uint32_t* count;          // shared [kGroupsPerBlock]
+  int64_t begin, end;       // the block's flat candidate range
+  int64_t chunk;            // candidates per group
+};
+
+// One flushed (row, key, n) triple: merge and finalise when complete.  A
+// row split between groups first merges in the block's shared slot; only
+// the group that completes the block's part of the row goes on to the
+// global key / arrival counter (so a long row costs one global merge per
+// block, not one per group).
 template <RowMode M>
 __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32_t r,
-                          int64_t row_len, unsigned long long key, int64_t n, int sub) {
+                          int64_t row_b, int64_t row_e, unsigned long long key, int64_t n,
+                          int sub, const BlockSlots& bs) {
   if (sub != 0 || n <= 0) return;
+  const int64_t row_len = row_e - row_b;
   if (n == row_len) {  // the group saw the whole row: no merge needed
     finalize_row<M>(p, rows_tab, r, key);
     return;
+  }
+  const int64_t lb = max(row_b, bs.begin), le = min(row_e, bs.end);
+  const int64_t local = le - lb;
+  if (n < local && lb >= bs.begin) {  // shared with other groups of this block
+    const int slot = (int)((lb - bs.begin) / bs.chunk);
+    atomicMax(bs.key + slot, key);
+    __threadfence_block();
+    const uint32_t before = atomicAdd(bs.count + slot, (uint32_t)n);
+    if ((int64_t)before + n != local) return;
+    __threadfence_block();
+    key = atomicExch(bs.key + slot, 0ull);
+    n = local;
+    if (n == row_len) {  // the row lies inside this block
+      finalize_row<M>(p, rows_tab, r, key);
+      return;
+    }
   }
   if (key != kKeyNone) atomicMax(p.keys + r, key);
   __threadfence();
@@ -243,6 +276,20 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     if (chunk < 4) chunk = 4;
   }
 
+  __shared__ unsigned long long s_slot_key[kGroupsPerBlock];
+  __shared__ uint32_t s_slot_count[kGroupsPerBlock];
+  if (threadIdx.x < kGroupsPerBlock) {
+    s_slot_key[threadIdx.x] = 0ull;
+    s_slot_count[threadIdx.x] = 0u;
+  }
+  __syncthreads();
+  BlockSlots bs;
+  bs.key = s_slot_key;
+  bs.count = s_slot_count;
+  bs.chunk = chunk;
+  bs.begin = min(total, (int64_t)blockIdx.x * kGroupsPerBlock * chunk);
+  bs.end = min(total, bs.begin + (int64_t)kGroupsPerBlock * chunk);
+
   const int lane = threadIdx.x & 31;
   const int sub = lane & 7;
   const unsigned gmask = 0xFFu << (lane & ~7);
@@ -267,7 +314,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     for (int64_t c = c_begin; c < c_end;) {
       // advance to the row that holds c (rows with no candidates are skipped)
       if (c >= row_e) {
-        flush_row<M>(p, rows_tab, r, row_e - row_b, best, seen, sub);
+        flush_row<M>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
         best = kKeyNone;
         seen = 0;
         while (c >= row_e && r + 1 < p.rows) {
@@ -327,7 +374,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
       seen += n_here;
       c += n_here;
     }
-    flush_row<M>(p, rows_tab, r, row_e - row_b, best, seen, sub);
+    flush_row<M>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
   }
 
   // Last block out (CSR mode; DFA offsets are built in-kernel and cannot be
