@@ -88,15 +88,40 @@ int mfref_linear_f32(const float* x, const float* w, std::uint64_t rows,
 
 // The reference CPU path for a ragged batch: per row, linear_f32 over every
 // vocab row of the FP32 embedding, then the masked argmax over the row's CSR
-// candidates.  Rows are split over `threads` std::threads.
+// candidates.  With at least as many rows as threads, rows are split over
+// `threads` std::threads; with fewer rows, each row's vocabulary is split
+// into `threads` slices, each a linear_f32 call on its slice of the
+// embedding (the same per-logit arithmetic).
 int mfref_full_logits_masked_head_csr(const float* hidden, const float* embedding_f32,
                                       const std::int32_t* offsets, const std::int32_t* ids,
                                       std::uint64_t rows, std::uint64_t hidden_size,
                                       std::uint64_t vocab, std::uint32_t* out_ids,
                                       float* out_best, int threads) {
   if (threads < 1) threads = 1;
-  if (static_cast<std::uint64_t>(threads) > rows) threads = static_cast<int>(rows);
   std::vector<int> codes(static_cast<std::size_t>(threads), 0);
+  if (rows < static_cast<std::uint64_t>(threads)) {
+    std::vector<float> logits(vocab);
+    for (std::uint64_t r = 0; r < rows; ++r) {
+      auto slice = [&](int t) {
+        const std::uint64_t v0 = vocab * t / threads, v1 = vocab * (t + 1) / threads;
+        if (v1 > v0) {
+          const int code = mfref_linear_f32(hidden + r * hidden_size,
+                                            embedding_f32 + v0 * hidden_size, 1, hidden_size,
+                                            v1 - v0, logits.data() + v0);
+          if (code != 0) codes[t] = code;
+        }
+      };
+      std::vector<std::thread> pool;
+      for (int t = 1; t < threads; ++t) pool.emplace_back(slice, t);
+      slice(0);
+      for (auto& th : pool) th.join();
+      for (int c : codes)
+        if (c != 0) return c;
+      masked_pick(logits.data(), ids + offsets[r], offsets[r + 1] - offsets[r], vocab,
+                  out_ids + r, out_best ? out_best + r : nullptr);
+    }
+    return 0;
+  }
   auto work = [&](int t) {
     std::vector<float> logits(vocab);
     const std::uint64_t b = rows * t / threads, e = rows * (t + 1) / threads;
@@ -111,13 +136,10 @@ int mfref_full_logits_masked_head_csr(const float* hidden, const float* embeddin
                   out_ids + r, out_best ? out_best + r : nullptr);
     }
   };
-  if (threads == 1) {
-    work(0);
-  } else {
-    std::vector<std::thread> pool;
-    for (int t = 0; t < threads; ++t) pool.emplace_back(work, t);
-    for (auto& th : pool) th.join();
-  }
+  std::vector<std::thread> pool;
+  for (int t = 1; t < threads; ++t) pool.emplace_back(work, t);
+  work(0);
+  for (auto& th : pool) th.join();
   for (int c : codes)
     if (c != 0) return c;
   return 0;

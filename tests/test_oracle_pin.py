@@ -159,3 +159,17 @@ def test_dfa_decode_oracle_follows_advance():
             x = O.widen(hid[s, b][None])
             logits = O.linear_f32(x, O.widen(emb[cands]))[0]
             assert t1[s, b] == cands[int(np.argmax(logits))]
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built (needs the reference sources)")
+def test_reference_vocab_split_mode_is_bit_identical():
+    """With fewer rows than threads the reference arm splits each row's
+    vocabulary over threads; every logit is still one linear_f32 dot."""
+    from market_sim_b200 import synth
+
+    emb = synth.embedding(41, vocab=3000)
+    hid = synth.hidden_states(41, 2)
+    off, ids = synth.ragged_batch(41, rows=2, kmax=900, vocab=3000)
+    a, b, _ = O.restricted_head_csr(hid, emb, off, ids)
+    c, d = O.ref_full_logits_masked_head_csr(hid, O.widen(emb), off, ids, threads=7)
+    assert np.array_equal(a, c) and np.array_equal(b.view(np.uint32), d.view(np.uint32))
