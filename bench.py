@@ -154,6 +154,19 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=device)
     emb, replicas, batches = make_inputs(rank, device)
     stream = torch.cuda.Stream(device)
+    if args.only:
+        # one secondary workload alone (for profiling captures)
+        identity = lambda x: x  # noqa: E731
+        fn = {"dense": lambda: bench_dense(emb, replicas, device, world, rank, stream,
+                                           lambda: dist.barrier() if world > 1 else None, identity),
+              "decode": lambda: bench_decode(emb, replicas[0], device, rank, stream, identity),
+              "ksweep": lambda: bench_k_sweep(replicas, device, stream)}[args.only]
+        res = fn()
+        if rank == 0:
+            print(json.dumps({"only": args.only, **res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     out_ids = torch.empty(ROWS, dtype=torch.int32, device=device)
     out_sc = torch.empty(ROWS, dtype=torch.float32, device=device)
     ws = torch.zeros(head.head_workspace_bytes(ROWS), dtype=torch.uint8, device=device)
@@ -613,6 +626,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--only", choices=["dense", "decode", "ksweep"],
+                    help="run one secondary workload alone and print its result (profiling)")
     ap.add_argument("--sweep", action="store_true",
                     help="also run the 10k-row K sweep (config 2 throughput; slower to set up)")
     ap.add_argument("--no-secondary", action="store_true",
