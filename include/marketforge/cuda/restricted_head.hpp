@@ -27,6 +27,15 @@ namespace marketforge::cuda {
     DeviceBuffer& workspace, std::uint64_t rows, std::uint64_t hidden_size,
     std::uint64_t vocabulary_size, StreamHandle stream) noexcept;
 
+// The same with the final RMSNorm fused in front: hidden holds the last
+// layer's un-normalised rows, gamma the norm weight fp16 [hidden_size]
+// (replaces rms_norm_f16 + the head, src/cuda/smollm2.cu:474-492).
+[[nodiscard]] Status restricted_output_head_csr_rmsnorm_f16(
+    const DeviceBuffer& hidden, const DeviceBuffer& gamma, float epsilon,
+    const DeviceBuffer& embedding, const DeviceBuffer& offsets, const DeviceBuffer& ids,
+    DeviceBuffer& token_ids, DeviceBuffer& scores, DeviceBuffer& workspace, std::uint64_t rows,
+    std::uint64_t hidden_size, std::uint64_t vocabulary_size, StreamHandle stream) noexcept;
+
 // `steps` device DFA steps (allowed-set lookup, head, advance; TokenDfa's
 // CSR: state_offsets / arc_tokens / arc_next).  state_trace u32
 // [steps + 1, batch] with row 0 = initial states; token_trace u32 [steps, batch].

@@ -124,6 +124,21 @@ MF_API mf_status mf_head_restricted_csr_f16(const void* hidden, uint64_t hidden_
                                      uint64_t rows, uint64_t hidden_size,
                                      uint64_t vocab, void* stream);
 
+/* The same head with the decoder's final RMSNorm fused in front: `hidden`
+ * holds the last layer's un-normalised rows (fp16 [rows, hidden_size]) and
+ * gamma the norm weight (fp16 [hidden_size], 16-byte aligned).  Each row is
+ * normalised in registers as rms_norm_f16 (src/cuda/rms_norm.cu:69-100)
+ * followed by the head would see it: inv = 1 / sqrt(mean(x^2) + eps) in
+ * FP32, h = fp16(x * inv * w).  Replaces the rms_norm_f16 launch before
+ * restricted_output_head_f16 (src/cuda/smollm2.cu:474-492).  eps must be
+ * finite and > 0 (rms_norm_f32's rule, src/cpu/operators.cpp:498-501). */
+MF_API mf_status mf_head_restricted_csr_rmsnorm_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* gamma, uint64_t gamma_bytes, float eps,
+    const void* embedding, uint64_t embedding_bytes, const void* offsets, uint64_t offsets_bytes,
+    const void* ids, uint64_t ids_bytes, void* out_ids, uint64_t out_ids_bytes, void* out_scores,
+    uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes, uint64_t rows,
+    uint64_t hidden_size, uint64_t vocab, void* stream);
+
 /* ---- device-resident DFA: allowed-set lookup + head + advance ------------
  *
  * The DFA is CSR over states, the flat form of TokenDfa/ActionDfa's

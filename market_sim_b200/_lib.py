@@ -39,6 +39,9 @@ _SIGNATURES = {
 _SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
                                                      _U64, _P, _U64, _U64, _U64, _U64, _P]
 
+_SIGNATURES["mf_head_restricted_csr_rmsnorm_f16"] = [_P, _U64, _P, _U64, ctypes.c_float, _P, _U64,
+                                                     _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
+                                                     _U64, _U64, _U64, _U64, _P]
 _SIGNATURES["mf_dense_head_f16"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
                                     _U64, _U64, _U64, _U64, _P]
 _SIGNATURES["mf_dense_selftest_wait_timeout"] = [_P, ctypes.POINTER(ctypes.c_uint32),

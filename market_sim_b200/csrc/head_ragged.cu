@@ -56,6 +56,10 @@ struct RaggedParams {
   uint32_t rows;
   uint32_t hidden_size;
   uint32_t vocab;
+  // Fused final RMSNorm (optional): when gamma is set, `hidden` holds the
+  // un-normalised rows and each is normalised in registers first.
+  const __half* gamma;
+  float eps;
 };
 
 constexpr int kThreads = 256;
@@ -134,14 +138,69 @@ __device__ __forceinline__ void load_hidden_fast(const __half* hidden, uint32_t 
   for (int k = 0; k < kFastChunksPerLane; ++k) h[k] = ld_v4(row + sub + 8 * k);
 }
 
+// Fused final RMSNorm of the row held in h (fast path): what the reference's
+// rms_norm_f16 (src/cuda/rms_norm.cu:69-100) would store, computed in FP32
+// and rounded to fp16: inv = 1 / sqrt(mean(x^2) + eps), h = fp16(x * inv * w)
+// (the order of src/cpu/operators.cpp:522-535).
+__device__ __forceinline__ void rms_norm_fast(const __half* gamma, float eps, int sub,
+                                              unsigned gmask, uint4 (&h)[kFastChunksPerLane]) {
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kFastChunksPerLane; ++k) {
+    const uint32_t w[4] = {h[k].x, h[k].y, h[k].z, h[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  ss = group8_sum(ss, gmask);
+  const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + eps);
+  const uint4* g = reinterpret_cast<const uint4*>(gamma);
+#pragma unroll
+  for (int k = 0; k < kFastChunksPerLane; ++k) {
+    const uint4 gv = ld_v4(g + sub + 8 * k);
+    uint32_t w[4] = {h[k].x, h[k].y, h[k].z, h[k].w};
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+      const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
+      w[j] = *reinterpret_cast<const uint32_t*>(&o);
+    }
+    h[k] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// inv_rms of hidden row r for the generic path (1 when not normalising).
+__device__ float row_inv_rms(const RaggedParams& p, uint32_t r, int sub, unsigned gmask) {
+  if (p.gamma == nullptr) return 1.f;
+  const __half* x = p.hidden + (size_t)r * p.hidden_size;
+  float ss = 0.f;
+  for (uint32_t f = sub; f < p.hidden_size; f += 8) {
+    const float v = __half2float(x[f]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = group8_sum(ss, gmask);
+  return 1.0f / sqrtf(ss / (float)p.hidden_size + p.eps);
+}
+
 // Dot product of hidden row r with embedding row t by one 8-lane group:
-// generic path for any width (used by the small known-answer shapes).
-__device__ float group_dot_generic(const __half* hidden, const __half* emb, uint32_t r,
-                                   uint32_t t, uint32_t width, int sub, unsigned gmask) {
+// generic path for any width (used by the small known-answer shapes).  With
+// a gamma, the hidden element is normalised and rounded to fp16 first.
+__device__ float group_dot_generic(const RaggedParams& p, uint32_t r, uint32_t t, float inv,
+                                   int sub, unsigned gmask) {
+  const uint32_t width = p.hidden_size;
   float a = 0.f;
-  const __half* h = hidden + (size_t)r * width;
-  const __half* e = emb + (size_t)t * width;
-  for (uint32_t f = sub; f < width; f += 8) a = fmaf(__half2float(h[f]), __half2float(e[f]), a);
+  const __half* h = p.hidden + (size_t)r * width;
+  const __half* e = p.embedding + (size_t)t * width;
+  for (uint32_t f = sub; f < width; f += 8) {
+    float hv = __half2float(h[f]);
+    if (p.gamma != nullptr) hv = __half2float(__float2half_rn(hv * inv * __half2float(p.gamma[f])));
+    a = fmaf(hv, __half2float(e[f]), a);
+  }
   return group8_sum(a, gmask);
 }
 
@@ -198,7 +257,7 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
   }
 }
 
-template <RowMode M, bool kFast>
+template <RowMode M, bool kFast, bool kNorm = false>
 __global__ void __launch_bounds__(kThreads, 2)
 ragged_head_kernel(RaggedParams p, int64_t chunk) {
   extern __shared__ int32_t smem_rows[];  // DFA mode: rows + 1 starts, then rows arc bases
@@ -307,7 +366,13 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     if constexpr (M == RowMode::kDfa) arc_base = (int64_t)rows_tab.arc_base[r] - row_b;
 
     uint4 h[kFastChunksPerLane];
-    if (kFast) load_hidden_fast(p.hidden, r, sub, h);
+    float inv = 1.f;  // generic path: the row's inv_rms when normalising
+    if (kFast) {
+      load_hidden_fast(p.hidden, r, sub, h);
+      if (kNorm) rms_norm_fast(p.gamma, p.eps, sub, gmask, h);
+    } else if (kNorm) {
+      inv = row_inv_rms(p, r, sub, gmask);
+    }
     unsigned long long best = kKeyNone;
     int64_t seen = 0;
 
@@ -324,10 +389,16 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
         }
         if (c >= row_e || c < row_b) break;  // malformed offsets: stop
         if constexpr (M == RowMode::kDfa) arc_base = (int64_t)rows_tab.arc_base[r] - row_b;
-        if (kFast) load_hidden_fast(p.hidden, r, sub, h);
+        if (kFast) {
+          load_hidden_fast(p.hidden, r, sub, h);
+          if (kNorm) rms_norm_fast(p.gamma, p.eps, sub, gmask, h);
+        } else if (kNorm) {
+          inv = row_inv_rms(p, r, sub, gmask);
+        }
       }
       // up to two candidates of this row per iteration
-      const int64_t n_here = min(min(c_end, row_e) - c, (int64_t)2);
+      // (one in the fused-norm variant, whose row-change path needs the registers)
+      const int64_t n_here = min(min(c_end, row_e) - c, (int64_t)(kNorm && kFast ? 1 : 2));
       uint32_t t0, t1 = 0;
       if (M == RowMode::kCsr) {
         t0 = (uint32_t)cand[c];
@@ -365,9 +436,8 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
         s0 = group8_sum(a0 + a1, gmask);
         s1 = group8_sum(b0 + b1, gmask);
       } else {
-        s0 = v0 ? group_dot_generic(p.hidden, p.embedding, r, t0, p.hidden_size, sub, gmask) : 0.f;
-        if (n_here > 1)
-          s1 = v1 ? group_dot_generic(p.hidden, p.embedding, r, t1, p.hidden_size, sub, gmask) : 0.f;
+        s0 = v0 ? group_dot_generic(p, r, t0, inv, sub, gmask) : 0.f;
+        if (n_here > 1) s1 = v1 ? group_dot_generic(p, r, t1, inv, sub, gmask) : 0.f;
       }
       best = umax64(best, v0 ? make_key(s0, id0) : kKeyPoison);
       if (n_here > 1) best = umax64(best, v1 ? make_key(s1, id1) : kKeyPoison);
@@ -503,12 +573,12 @@ void split_workspace(void* ws, uint64_t rows, RaggedParams& p) {
 
 }  // namespace
 
-extern "C" mf_status mf_head_restricted_csr_f16(
+static mf_status csr_head(
     const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
     const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
     void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
     void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
-    uint64_t vocab, void* stream) {
+    uint64_t vocab, void* stream, const void* gamma, float eps) {
   if (rows == 0 || hidden_size == 0 || vocab == 0 || stream == nullptr)
     return fail(MF_INVALID_ARGUMENT);
   if (vocab > UINT32_MAX || hidden_size > UINT32_MAX || rows > (uint64_t)INT32_MAX - 1)
@@ -538,6 +608,8 @@ extern "C" mf_status mf_head_restricted_csr_f16(
   p.rows = (uint32_t)rows;
   p.hidden_size = (uint32_t)hidden_size;
   p.vocab = (uint32_t)vocab;
+  p.gamma = static_cast<const __half*>(gamma);
+  p.eps = eps;
   split_workspace(workspace, rows, p);
 
   const bool fast = fast_path(hidden, embedding, hidden_size);
@@ -550,11 +622,44 @@ extern "C" mf_status mf_head_restricted_csr_f16(
   int64_t chunk = (p.total + groups - 1) / groups;
   if (chunk < 1) chunk = 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (fast)
+  if (fast && p.gamma)
+    ragged_head_kernel<RowMode::kCsr, true, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+  else if (fast)
     ragged_head_kernel<RowMode::kCsr, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+  else if (p.gamma)
+    ragged_head_kernel<RowMode::kCsr, false, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
   else
     ragged_head_kernel<RowMode::kCsr, false><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
   return launch_status(cudaGetLastError());
+}
+
+extern "C" mf_status mf_head_restricted_csr_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
+    uint64_t vocab, void* stream) {
+  return csr_head(hidden, hidden_bytes, embedding, embedding_bytes, offsets, offsets_bytes, ids,
+                  ids_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes, workspace,
+                  workspace_bytes, rows, hidden_size, vocab, stream, nullptr, 0.f);
+}
+
+extern "C" mf_status mf_head_restricted_csr_rmsnorm_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* gamma, uint64_t gamma_bytes, float eps,
+    const void* embedding, uint64_t embedding_bytes, const void* offsets, uint64_t offsets_bytes,
+    const void* ids, uint64_t ids_bytes, void* out_ids, uint64_t out_ids_bytes, void* out_scores,
+    uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes, uint64_t rows,
+    uint64_t hidden_size, uint64_t vocab, void* stream) {
+  // rms_norm_f32's own checks (src/cpu/operators.cpp:498-501): finite eps > 0
+  if (!(eps > 0.f) || !(eps < 3.0e38f) || gamma == nullptr)
+    return fail(MF_INVALID_ARGUMENT);
+  if (gamma_bytes != hidden_size * 2 || (uintptr_t)gamma % 16 != 0) return fail(MF_INVALID_ARGUMENT);
+  if (gamma == hidden || gamma == embedding || gamma == offsets || gamma == ids ||
+      gamma == out_ids || gamma == out_scores || gamma == workspace)
+    return fail(MF_INVALID_ARGUMENT);
+  return csr_head(hidden, hidden_bytes, embedding, embedding_bytes, offsets, offsets_bytes, ids,
+                  ids_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes, workspace,
+                  workspace_bytes, rows, hidden_size, vocab, stream, gamma, eps);
 }
 
 namespace {

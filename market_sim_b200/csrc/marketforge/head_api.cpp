@@ -70,6 +70,19 @@ Status restricted_output_head_csr_f16(const DeviceBuffer& hidden, const DeviceBu
       workspace.size_bytes(), rows, hidden_size, vocabulary_size, st(stream)));
 }
 
+Status restricted_output_head_csr_rmsnorm_f16(
+    const DeviceBuffer& hidden, const DeviceBuffer& gamma, float epsilon,
+    const DeviceBuffer& embedding, const DeviceBuffer& offsets, const DeviceBuffer& ids,
+    DeviceBuffer& token_ids, DeviceBuffer& scores, DeviceBuffer& workspace, std::uint64_t rows,
+    std::uint64_t hidden_size, std::uint64_t vocabulary_size, StreamHandle stream) noexcept {
+  return to_status(mf_head_restricted_csr_rmsnorm_f16(
+      ca(hidden), hidden.size_bytes(), ca(gamma), gamma.size_bytes(), epsilon, ca(embedding),
+      embedding.size_bytes(), ca(offsets), offsets.size_bytes(), ca(ids), ids.size_bytes(),
+      ma(token_ids), token_ids.size_bytes(), scores.address().valid() ? ma(scores) : nullptr,
+      scores.size_bytes(), ma(workspace), workspace.size_bytes(), rows, hidden_size,
+      vocabulary_size, st(stream)));
+}
+
 Status dfa_decode_f16(const DeviceBuffer& hidden, const DeviceBuffer& embedding,
                       const DeviceBuffer& state_offsets, const DeviceBuffer& arc_tokens,
                       const DeviceBuffer& arc_next, DeviceBuffer& state_trace,

@@ -269,6 +269,19 @@ def restricted_output_head_csr_f16_noalloc(hidden: Buffer, embedding: Buffer, of
         rows, hidden_size, vocabulary_size, _sp(stream)))
 
 
+def restricted_output_head_csr_rmsnorm_f16(hidden: Buffer, gamma: Buffer, eps: float,
+                                           embedding: Buffer, offsets: Buffer, ids: Buffer,
+                                           token_ids: Buffer, scores: Optional[Buffer],
+                                           workspace: Buffer, rows: int, hidden_size: int,
+                                           vocabulary_size: int, stream) -> Status:
+    """Ragged head with the final RMSNorm fused in front (hidden = the last
+    layer's un-normalised rows, gamma = the norm weight)."""
+    return _status(lib.mf_head_restricted_csr_rmsnorm_f16(
+        *_pb(hidden), *_pb(gamma), float(eps), *_pb(embedding), *_pb(offsets), *_pb(ids),
+        *_pb(token_ids), *_pb(scores), *_pb(workspace), rows, hidden_size, vocabulary_size,
+        _sp(stream)))
+
+
 def dfa_head_step_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer,
                       arc_tokens: Buffer, arc_next: Buffer, states_in: Buffer,
                       states_out: Buffer, tokens: Buffer, scores: Optional[Buffer],

@@ -390,3 +390,51 @@ def test_host_pipeline_matches_direct_calls(mf, emb_full):
         got, sc, _ = _csr_call(mf, h, e_dev, off, ids)
         assert np.array_equal(oi.numpy().view(np.uint32), got)
         assert np.array_equal(osc.numpy().view(np.uint32), sc.view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,kmax,hs", [(64, 4096, 576), (9, 40, 64)])
+def test_fused_rmsnorm_head_vs_oracle(mf, O, rows, kmax, hs):
+    """Final RMSNorm fused into the head: equals the oracle's rms_norm_f32
+    (src/cpu/operators.cpp:489-537), rounded to fp16 as rms_norm_f16 stores
+    it, followed by the restricted head (margin rule for near-ties)."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    vocab = 49_152 if hs == 576 else 3000
+    e = synth.embedding(61 + hs, vocab=vocab, hidden=hs)
+    x = (synth.normal(62, 1, rows * hs) * 3).astype(np.float32).astype(np.float16).reshape(rows, hs)
+    g = synth.normal(63, 2, hs, 1.0, 0.02).astype(np.float32).astype(np.float16)
+    off, ids = synth.ragged_batch(64, rows=rows, kmax=kmax, vocab=vocab)
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ws = torch.zeros(mf.head_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    st = mf.restricted_output_head_csr_rmsnorm_f16(to_dev(x), to_dev(g), 1e-5, to_dev(e),
+                                                   to_dev(off), to_dev(ids), out, sc, ws, rows, hs,
+                                                   vocab, _stream())
+    assert st.ok(), st
+    torch.cuda.synchronize()
+    h16 = O.rms_norm_f32(O.widen(x), O.widen(g), 1e-5).astype(np.float16)
+    oid, obest, oru = O.restricted_head_csr(h16, e, off, ids)
+    check_head_parity(_u32(out), sc.cpu().numpy(), oid, obest, oru)
+    assert int(ws.sum()) == 0
+
+
+def test_fused_rmsnorm_rejects(mf):
+    import torch
+
+    E = mf.ErrorCode
+    rows, hs, v = 2, 576, 100
+    x = torch.zeros((rows, hs), dtype=torch.float16, device="cuda")
+    g = torch.ones(hs, dtype=torch.float16, device="cuda")
+    e = torch.zeros((v, hs), dtype=torch.float16, device="cuda")
+    off = to_dev(np.array([0, 1, 2], np.int32))
+    ids = to_dev(np.array([3, 4], np.int32))
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(mf.head_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    s = _stream()
+    f = mf.restricted_output_head_csr_rmsnorm_f16
+    assert f(x, g, 0.0, e, off, ids, out, None, ws, rows, hs, v, s).code == E.invalid_argument
+    assert f(x, g, float("nan"), e, off, ids, out, None, ws, rows, hs, v, s).code == E.invalid_argument
+    assert f(x, g[:100], 1e-5, e, off, ids, out, None, ws, rows, hs, v, s).code == E.invalid_argument
+    assert f(x, g, 1e-5, e, off, ids, out, None, ws, rows, hs, v, s).ok()
