@@ -247,6 +247,14 @@ MF_API mf_status mf_pipeline_create(mf_pipeline** pipeline, const void* embeddin
 MF_API mf_status mf_pipeline_submit(mf_pipeline* pipeline, const void* hidden, uint64_t rows,
                                     const void* offsets, const void* ids, uint64_t total_ids,
                                     void* out_ids, void* out_scores, uint64_t* ticket);
+/* One batch as a single packed host buffer: hidden fp16 [rows, hidden_size],
+ * then offsets int32 [rows + 1], then ids int32 [total_ids], back to back
+ * (batch_bytes must equal rows*hidden_size*2 + (rows+1)*4 + total_ids*4);
+ * `out` receives ids u32 [rows] then scores f32 [rows].  One copy each way
+ * instead of up to five. */
+MF_API mf_status mf_pipeline_submit_packed(mf_pipeline* pipeline, const void* batch,
+                                           uint64_t batch_bytes, uint64_t rows,
+                                           uint64_t total_ids, void* out, uint64_t* ticket);
 MF_API mf_status mf_pipeline_wait(mf_pipeline* pipeline, uint64_t ticket);
 MF_API mf_status mf_pipeline_synchronize(mf_pipeline* pipeline);
 /* The pipeline's streams: 0 = copy-in, 1 = compute, 2 = copy-out. */

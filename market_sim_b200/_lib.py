@@ -51,6 +51,7 @@ _SIGNATURES["mf_decode_keys"] = [_P, _U64, _P, _U64, _P, _U64, _U64, _P]
 _SIGNATURES["mf_pipeline_create"] = [ctypes.POINTER(_P), _P, _U64, _U64, _U64, _U64, _U64,
                                      ctypes.c_uint32]
 _SIGNATURES["mf_pipeline_submit"] = [_P, _P, _U64, _P, _P, _U64, _P, _P, ctypes.POINTER(_U64)]
+_SIGNATURES["mf_pipeline_submit_packed"] = [_P, _P, _U64, _U64, _U64, _P, ctypes.POINTER(_U64)]
 _SIGNATURES["mf_pipeline_wait"] = [_P, _U64]
 _SIGNATURES["mf_pipeline_synchronize"] = [_P]
 

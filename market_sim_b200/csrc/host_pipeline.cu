@@ -14,11 +14,13 @@
 
 namespace {
 
+// A slot holds one batch in the packed layout of mf_pipeline_submit_packed:
+// `in` = hidden fp16 [rows, H] | offsets int32 [rows + 1] | ids int32 [total]
+// and `out` = ids u32 [rows] | scores f32 [rows], so a packed host batch moves
+// with one copy each way.
 struct Slot {
-  void* hidden = nullptr;
-  void* offsets = nullptr;
-  void* ids = nullptr;
-  void* out = nullptr;  // u32 ids [max_rows] then f32 scores [max_rows]
+  void* in = nullptr;
+  void* out = nullptr;
   cudaEvent_t loaded = nullptr, ran = nullptr, done = nullptr;
   bool used = false;
 };
@@ -33,6 +35,10 @@ struct mf_pipeline {
   void* workspace = nullptr;
   std::vector<Slot> slots;
   uint64_t submitted = 0;
+
+  uint64_t packed_bytes(uint64_t rows, uint64_t total_ids) const {
+    return rows * hidden_size * 2 + (rows + 1) * 4 + total_ids * 4;
+  }
 };
 
 namespace {
@@ -46,9 +52,7 @@ void release(mf_pipeline* p) {
   cudaGetDevice(&prev);
   cudaSetDevice(p->device);
   for (auto& s : p->slots) {
-    cudaFree(s.hidden);
-    cudaFree(s.offsets);
-    cudaFree(s.ids);
+    cudaFree(s.in);
     cudaFree(s.out);
     if (s.loaded) cudaEventDestroy(s.loaded);
     if (s.ran) cudaEventDestroy(s.ran);
@@ -90,9 +94,7 @@ extern "C" mf_status mf_pipeline_create(mf_pipeline** out, const void* embedding
   if (e == cudaSuccess) e = cudaMemset(p->workspace, 0, ws);
   p->slots.resize(depth);
   for (auto& s : p->slots) {
-    if (e == cudaSuccess) e = cudaMalloc(&s.hidden, max_rows * hidden_size * 2);
-    if (e == cudaSuccess) e = cudaMalloc(&s.offsets, (max_rows + 1) * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&s.ids, (max_ids ? max_ids : 1) * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&s.in, p->packed_bytes(max_rows, max_ids));
     if (e == cudaSuccess) e = cudaMalloc(&s.out, max_rows * 8);
     for (cudaEvent_t* ev : {&s.loaded, &s.ran, &s.done})
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
@@ -105,6 +107,43 @@ extern "C" mf_status mf_pipeline_create(mf_pipeline** out, const void* embedding
   return st_ok();
 }
 
+namespace {
+
+// Everything after the copy-in of one batch into slot `s`: the head on the
+// compute stream, then the copy-out: one copy of ids + scores when `joined`
+// (the caller's packed output buffer), else one per buffer.  Adjacent
+// addresses alone do not make a buffer packed: two pinned allocations can be
+// neighbours, and one copy across both is invalid.
+mf_status run_and_return(mf_pipeline* p, Slot& s, uint64_t rows, uint64_t total_ids,
+                         void* out_ids, void* out_scores, bool joined, uint64_t* ticket) {
+  cudaError_t e = cudaEventRecord(s.loaded, p->s_in);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_run, s.loaded, 0);
+  if (e != cudaSuccess) return st_rt(e);
+  const uint64_t hb = rows * p->hidden_size * 2;
+  char* in = static_cast<char*>(s.in);
+  char* out = static_cast<char*>(s.out);
+  const mf_status h = mf_head_restricted_csr_f16(
+      in, hb, p->embedding, p->embedding_bytes, in + hb, (rows + 1) * 4,
+      total_ids ? in + hb + (rows + 1) * 4 : nullptr, total_ids * 4, out, rows * 4,
+      out + rows * 4, rows * 4, p->workspace, mf_head_workspace_bytes(rows), rows,
+      p->hidden_size, p->vocab, p->s_run);
+  if (h.code != MF_OK) return h;
+  e = cudaEventRecord(s.ran, p->s_run);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_out, s.ran, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out_ids, out, rows * (joined ? 8 : 4), cudaMemcpyDeviceToHost, p->s_out);
+  if (e == cudaSuccess && out_scores && !joined)
+    e = cudaMemcpyAsync(out_scores, out + rows * 4, rows * 4, cudaMemcpyDeviceToHost, p->s_out);
+  if (e == cudaSuccess) e = cudaEventRecord(s.done, p->s_out);
+  if (e != cudaSuccess) return st_rt(e);
+  s.used = true;
+  if (ticket) *ticket = p->submitted;
+  ++p->submitted;
+  return st_ok();
+}
+
+}  // namespace
+
 extern "C" mf_status mf_pipeline_submit(mf_pipeline* p, const void* hidden, uint64_t rows,
                                         const void* offsets, const void* ids, uint64_t total_ids,
                                         void* out_ids, void* out_scores, uint64_t* ticket) {
@@ -116,32 +155,32 @@ extern "C" mf_status mf_pipeline_submit(mf_pipeline* p, const void* hidden, uint
   cudaError_t e = cudaSuccess;
   if (s.used) e = cudaStreamWaitEvent(p->s_in, s.done, 0);  // slot's previous batch is home
   const uint64_t hb = rows * p->hidden_size * 2;
-  if (e == cudaSuccess) e = cudaMemcpyAsync(s.hidden, hidden, hb, cudaMemcpyHostToDevice, p->s_in);
+  char* in = static_cast<char*>(s.in);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(in, hidden, hb, cudaMemcpyHostToDevice, p->s_in);
   if (e == cudaSuccess)
-    e = cudaMemcpyAsync(s.offsets, offsets, (rows + 1) * 4, cudaMemcpyHostToDevice, p->s_in);
+    e = cudaMemcpyAsync(in + hb, offsets, (rows + 1) * 4, cudaMemcpyHostToDevice, p->s_in);
   if (e == cudaSuccess && total_ids)
-    e = cudaMemcpyAsync(s.ids, ids, total_ids * 4, cudaMemcpyHostToDevice, p->s_in);
-  if (e == cudaSuccess) e = cudaEventRecord(s.loaded, p->s_in);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_run, s.loaded, 0);
+    e = cudaMemcpyAsync(in + hb + (rows + 1) * 4, ids, total_ids * 4, cudaMemcpyHostToDevice,
+                        p->s_in);
   if (e != cudaSuccess) return st_rt(e);
-  char* out = static_cast<char*>(s.out);
-  const mf_status h = mf_head_restricted_csr_f16(
-      s.hidden, hb, p->embedding, p->embedding_bytes, s.offsets, (rows + 1) * 4,
-      total_ids ? s.ids : nullptr, total_ids * 4, out, rows * 4, out + p->max_rows * 4, rows * 4,
-      p->workspace, mf_head_workspace_bytes(rows), rows, p->hidden_size, p->vocab, p->s_run);
-  if (h.code != MF_OK) return h;
-  e = cudaEventRecord(s.ran, p->s_run);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_out, s.ran, 0);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(out_ids, out, rows * 4, cudaMemcpyDeviceToHost, p->s_out);
-  if (e == cudaSuccess && out_scores)
-    e = cudaMemcpyAsync(out_scores, out + p->max_rows * 4, rows * 4, cudaMemcpyDeviceToHost,
-                        p->s_out);
-  if (e == cudaSuccess) e = cudaEventRecord(s.done, p->s_out);
+  return run_and_return(p, s, rows, total_ids, out_ids, out_scores, false, ticket);
+}
+
+extern "C" mf_status mf_pipeline_submit_packed(mf_pipeline* p, const void* batch,
+                                               uint64_t batch_bytes, uint64_t rows,
+                                               uint64_t total_ids, void* out,
+                                               uint64_t* ticket) {
+  if (p == nullptr || batch == nullptr || out == nullptr || rows == 0)
+    return mf_status{MF_INVALID_ARGUMENT, 0};
+  if (rows > p->max_rows || total_ids > p->max_ids) return mf_status{MF_RESOURCE_LIMIT, 0};
+  if (batch_bytes != p->packed_bytes(rows, total_ids)) return mf_status{MF_INVALID_ARGUMENT, 0};
+  Slot& s = p->slots[p->submitted % p->slots.size()];
+  cudaError_t e = cudaSuccess;
+  if (s.used) e = cudaStreamWaitEvent(p->s_in, s.done, 0);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(s.in, batch, batch_bytes, cudaMemcpyHostToDevice, p->s_in);
   if (e != cudaSuccess) return st_rt(e);
-  s.used = true;
-  if (ticket) *ticket = p->submitted;
-  ++p->submitted;
-  return st_ok();
+  return run_and_return(p, s, rows, total_ids, out, static_cast<char*>(out) + rows * 4, true,
+                        ticket);
 }
 
 extern "C" mf_status mf_pipeline_wait(mf_pipeline* p, uint64_t ticket) {

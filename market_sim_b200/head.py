@@ -382,7 +382,7 @@ class HostPipeline:
     must stay untouched until ``wait(ticket)`` returns.
     """
 
-    def __init__(self, embedding, max_rows: int, max_ids: int, depth: int = 2, device=None):
+    def __init__(self, embedding, max_rows: int, max_ids: int, depth: int = 6, device=None):
         self.embedding = embedding  # keeps the device table alive
         self.vocab, self.hidden_size = int(embedding.shape[0]), int(embedding.shape[1])
         self._p = ctypes.c_void_p()
@@ -415,6 +415,38 @@ class HostPipeline:
         if s.code:
             raise RuntimeError(f"mf_pipeline_submit failed: {_status(s)}")
         return self._ticket.value
+
+    @staticmethod
+    def pack(hidden, offsets, ids):
+        """One pinned uint8 host buffer holding hidden fp16 [rows, H], offsets
+        int32 [rows + 1] and ids int32 [total] back to back (the layout of
+        ``submit_packed``)."""
+        import torch
+
+        parts = [torch.as_tensor(x).contiguous().view(torch.uint8).reshape(-1)
+                 for x in (hidden, offsets, ids)]
+        buf = torch.empty(sum(p.numel() for p in parts), dtype=torch.uint8).pin_memory()
+        at = 0
+        for part in parts:
+            buf[at:at + part.numel()] = part
+            at += part.numel()
+        return buf
+
+    def submit_packed_ptrs(self, batch: int, batch_bytes: int, rows: int, total_ids: int,
+                           out: int) -> int:
+        """One packed batch (see ``pack``) at host address ``batch``; ``out``
+        receives ids u32 [rows] then scores f32 [rows].  One H2D and one D2H
+        copy per batch."""
+        s = lib.mf_pipeline_submit_packed(self._p, batch, batch_bytes, rows, total_ids, out,
+                                          self._ticket_ref)
+        if s.code:
+            raise RuntimeError(f"mf_pipeline_submit_packed failed: {_status(s)}")
+        return self._ticket.value
+
+    def submit_packed(self, batch, rows: int, total_ids: int, out) -> int:
+        """``batch`` from ``pack``; ``out`` a pinned host tensor of 8 * rows bytes."""
+        return self.submit_packed_ptrs(batch.data_ptr(), batch.numel() * batch.element_size(),
+                                       rows, total_ids, out.data_ptr())
 
     def wait(self, ticket: int) -> None:
         st = _status(lib.mf_pipeline_wait(self._p, ticket))

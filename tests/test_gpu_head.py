@@ -392,6 +392,34 @@ def test_host_pipeline_matches_direct_calls(mf, emb_full):
         assert np.array_equal(osc.numpy().view(np.uint32), sc.view(np.uint32))
 
 
+def test_host_pipeline_packed_batches(mf, emb_full):
+    """submit_packed (one H2D and one D2H copy per batch, varying row counts
+    and id totals, slots reused) equals direct device calls; a batch whose
+    byte count disagrees with its rows and ids is rejected."""
+    import torch
+
+    e, e_dev = emb_full
+    pipe = mf.HostPipeline(e_dev, 256, 600_000, depth=3)
+    cases = [_ragged_case(700 + i, rows, kmax) for i, (rows, kmax) in
+             enumerate([(256, 4096), (1, 1), (100, 300), (256, 4096), (7, 4096)])]
+    outs = []
+    for h, off, ids in cases:
+        b = mf.HostPipeline.pack(h, off, ids)
+        o = torch.empty(2 * len(h), dtype=torch.int32).pin_memory()
+        pipe.submit_packed(b, len(h), ids.size, o)
+        outs.append((b, o))
+    with pytest.raises(RuntimeError, match="invalid_argument"):
+        pipe.submit_packed_ptrs(outs[0][0].data_ptr(), outs[0][0].numel() - 4, 256,
+                                cases[0][2].size, outs[0][1].data_ptr())
+    pipe.synchronize()
+    for (h, off, ids), (_, o) in zip(cases, outs):
+        got, sc, _ = _csr_call(mf, h, e_dev, off, ids)
+        r = len(h)
+        assert np.array_equal(o.numpy()[:r].view(np.uint32), got)
+        assert np.array_equal(o.numpy()[r:].view(np.uint32), sc.view(np.uint32))
+    pipe.close()
+
+
 @pytest.mark.parametrize("rows,kmax,hs", [(64, 4096, 576), (9, 40, 64)])
 def test_fused_rmsnorm_head_vs_oracle(mf, O, rows, kmax, hs):
     """Final RMSNorm fused into the head: equals the oracle's rms_norm_f32
