@@ -6,19 +6,24 @@
 // greedy_select_f16 (src/cuda/greedy.cu:21-59, 237-279).  Here the scores
 // stay FP32 and only one packed (score, id) key per row leaves the SM.
 //
-// Tile = 128 hidden rows (M) x 256 vocabulary rows (N); K = hidden width in
-// 64-element (128-byte) chunks.  One CTA per SM, persistent:
-//   * CTA (m, q) keeps hidden tile m resident in shared memory (loaded once
-//     by TMA, 128-byte swizzle, K-major) and walks vocabulary tiles
-//     n = q, q + Q, q + 2Q, ...  The CTAs that share an n sequence run
-//     together, so each embedding tile comes from DRAM once and from L2 for
-//     the other hidden tiles;
-//   * warp 0 (one lane) streams embedding chunks with TMA into a 2-stage
-//     ring (no multicast: a plain tiled load of this GPU's memory);
-//   * warp 1 owns TMEM (512 columns = two 128 x 256 f32 accumulators) and
-//     one lane issues tcgen05.mma.kind::f16 (4 per chunk), committing to
-//     the ring's "empty" barriers and to the accumulator's "full" barrier;
-//   * warps 2-9 drain the other accumulator with tcgen05.ld while the next
+// Tile = 256 hidden rows (M) x 256 vocabulary rows (N) on a pair of CTAs
+// (a 2-CTA cluster, tcgen05 cta_group::2); K = hidden width in 64-element
+// (128-byte) chunks.  One CTA per SM, persistent:
+//   * pair (m, q) keeps hidden tile m resident in shared memory, 128 rows in
+//     each CTA (loaded once by TMA, 128-byte swizzle, K-major), and walks
+//     vocabulary tiles n = q, q + Q, q + 2Q, ...; each CTA loads 128 of a
+//     tile's 256 embedding rows, so an embedding row crosses L2 -> SM once
+//     per 256 hidden rows.  The pairs that share an n sequence run together,
+//     so each embedding tile comes from DRAM once and from L2 for the others;
+//   * warp 0 (one lane) of each CTA streams its half of the embedding chunks
+//     with TMA into a 4-stage ring (no multicast: a plain tiled load of this
+//     GPU's memory, completing on the leader CTA's barrier);
+//   * warp 1 of both CTAs owns TMEM (512 columns = two 128 x 256 f32
+//     accumulators per CTA); one lane of the leader CTA issues
+//     tcgen05.mma.cta_group::2.kind::f16 (M = 256, N = 256; 4 per chunk),
+//     whose commits arrive on the ring's "empty" and the accumulator's
+//     "full" barriers of both CTAs;
+//   * warps 2-9 of each CTA drain its accumulator with tcgen05.ld while the next
 //     tile accumulates: thread = one hidden row and half of the tile's 256
 //     columns; per 64 columns a NaN-ignoring max tree, and only when it beats
 //     the running best, a search for the lowest column holding it (columns
@@ -44,13 +49,14 @@
 namespace mfb {
 namespace dense {
 
-constexpr int kBM = 128;          // hidden rows per tile (MMA M)
+constexpr int kBM = 128;          // hidden rows per CTA (MMA M = 2 x kBM per pair)
 constexpr int kBN = 256;          // vocabulary rows per tile (MMA N)
+constexpr int kBNHalf = kBN / 2;  // embedding rows each CTA of the pair loads
 constexpr int kBK = 64;           // K elements per chunk (one 128-byte swizzle atom)
 constexpr int kMaxKChunks = 9;    // hidden width up to 576
-constexpr int kStages = 2;        // embedding chunks in flight
-constexpr int kAChunkBytes = kBM * kBK * 2;  // 16 KB
-constexpr int kBChunkBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kStages = 4;        // embedding chunks in flight
+constexpr int kAChunkBytes = kBM * kBK * 2;      // 16 KB
+constexpr int kBChunkBytes = kBNHalf * kBK * 2;  // 16 KB per CTA
 constexpr int kEpiWarps = 8;      // two per TMEM lane quadrant, each on half the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA, epilogue warps
 constexpr uint32_t kTmemCols = 512;
@@ -60,8 +66,8 @@ struct Smem {  // offsets inside the 1024-aligned dynamic shared memory
   static constexpr int a = 0;
   static constexpr int b = kMaxKChunks * kAChunkBytes;             // 147,456
   static constexpr int bars = b + kStages * kBChunkBytes;          // 212,992
-  // barriers: a_full, b_full[2], b_empty[2], acc_full[2], acc_empty[2], drain
-  static constexpr int n_bars = 10;
+  // barriers: a_full, b_full[S], b_empty[S], acc_full[2], acc_empty[2], drain
+  static constexpr int n_bars = 2 * kStages + 6;
   static constexpr int tmem_slot = bars + n_bars * 8;
   static constexpr int abort_flag = tmem_slot + 4;
   // u32[kStages + 1]: TMA loads issued per stage, then 1 if the hidden tile was
@@ -75,7 +81,7 @@ struct Params {
   uint32_t k_chunks;    // hidden width / 64
   uint32_t vocab_rows;  // rows of this vocabulary shard
   uint32_t vocab_begin; // global id of shard row 0
-  uint32_t m_tiles, n_tiles, per_m;
+  uint32_t m_tiles, n_tiles, per_m;  // m_tiles: 256-row hidden tiles (pairs)
   unsigned long long* keys;  // workspace: rows keys
   uint32_t* control;         // workspace: done counter, error word
   unsigned long long* out_keys;
@@ -98,8 +104,25 @@ __device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
                : "memory");
 }
 
-__device__ __forceinline__ void bar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (any CTA of the cluster).
+__device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// All threads of both CTAs of the pair; both CTAs always reach it (every
+// wait before it is bounded).
+__device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
 }
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -125,12 +148,15 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// Tiled load into this CTA's shared memory whose completion is counted on
+// `leader_bar`, a shared::cluster address of the leader CTA's barrier
+// (cta_group::2 lets the barrier live in the peer CTA).  No multicast.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t bar) {
+                                            uint32_t leader_bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(leader_bar)
       : "memory");
 }
 
@@ -147,21 +173,33 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 }
 
 // Instruction descriptor for kind::f16: F32 accumulator, F16 A and B, both
-// K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+// K-major, N = 256, M = 256 (the pair's two 128-row halves).
+constexpr uint32_t kIdesc =
+    (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)((2 * kBM) >> 4) << 24);
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                         uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+// Arrives (once the MMAs issued so far complete) on the barrier at this
+// shared-memory offset in both CTAs of the pair.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+
+// Same, on this CTA's barrier only.
+__device__ __forceinline__ void mma_commit_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar)
                : "memory");
 }
@@ -182,7 +220,7 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
                   const __grid_constant__ CUtensorMap tm_emb, Params p) {
   extern __shared__ unsigned char smem_raw[];
@@ -192,19 +230,23 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
   const uint32_t bar0 = sbase + Smem::bars;
   const uint32_t a_full = bar0;
   auto b_full = [&](int s) { return bar0 + 8 * (1 + s); };
-  auto b_empty = [&](int s) { return bar0 + 8 * (3 + s); };
-  auto acc_full = [&](int b) { return bar0 + 8 * (5 + b); };
-  auto acc_empty = [&](int b) { return bar0 + 8 * (7 + b); };
-  const uint32_t drain = bar0 + 8 * 9;
+  auto b_empty = [&](int s) { return bar0 + 8 * (1 + kStages + s); };
+  auto acc_full = [&](int b) { return bar0 + 8 * (1 + 2 * kStages + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8 * (3 + 2 * kStages + b); };
+  const uint32_t drain = bar0 + 8 * (5 + 2 * kStages);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(sm + Smem::abort_flag);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Smem::tmem_slot);
   volatile uint32_t* issued = reinterpret_cast<volatile uint32_t*>(sm + Smem::issued);
   __shared__ uint32_t s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m = blockIdx.x % p.m_tiles;  // hidden tile
-  const uint32_t q = blockIdx.x / p.m_tiles;  // position in the vocabulary walk
+  uint32_t rank;  // 0 = leader (issues the MMAs), 1 = peer
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const uint32_t pair = blockIdx.x >> 1;
+  const uint32_t m = pair % p.m_tiles;  // 256-row hidden tile
+  const uint32_t q = pair / p.m_tiles;  // position in the vocabulary walk
   const uint32_t my_tiles = q < p.n_tiles ? (p.n_tiles - q + p.per_m - 1) / p.per_m : 0;
+  const bool leader = rank == 0;
 
   if (threadIdx.x == 0) {
     bar_init(a_full, 1);
@@ -214,34 +256,36 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
     }
     for (int b = 0; b < 2; ++b) {
       bar_init(acc_full(b), 1);
-      bar_init(acc_empty(b), kEpiWarps);  // one arrival per epilogue warp
+      bar_init(acc_empty(b), 2 * kEpiWarps);  // leader's: one arrival per epilogue warp of the pair
     }
     bar_init(drain, 1);
     *abort_flag = 0u;
     for (int s = 0; s <= kStages; ++s) issued[s] = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // TMEM: 512 columns, two 256-column accumulators
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+  if (warp == 1) {  // TMEM: 512 columns per CTA, two 256-column accumulators
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t chunks = p.k_chunks;
 
   if (warp == 0) {
     // ---- producer: hidden tile once, then the embedding chunks ----
+    // Both CTAs load their halves; the copies complete on the leader's
+    // barriers, whose expected byte counts (set by the leader) cover both.
     if (lane == 0 && my_tiles > 0 && !p.skip_loads) {
       issued[kStages] = 1u;  // the hidden tile
-      bar_expect_tx(a_full, chunks * kAChunkBytes);
+      if (leader) bar_expect_tx(a_full, 2 * chunks * kAChunkBytes);
       for (uint32_t kc = 0; kc < chunks; ++kc)
         tma_load_2d(sbase + Smem::a + kc * kAChunkBytes, &tm_hidden, (int)(kc * kBK),
-                    (int)(m * kBM), a_full);
+                    (int)(m * 2 * kBM + rank * kBM), mapa(a_full, 0));
       uint32_t it = 0;
       for (uint32_t t = 0; t < my_tiles && !*abort_flag; ++t) {
         const uint32_t n = q + t * p.per_m;
@@ -252,16 +296,16 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
             *abort_flag = 1u;
             break;
           }
-          bar_expect_tx(b_full(s), kBChunkBytes);
+          if (leader) bar_expect_tx(b_full(s), 2 * kBChunkBytes);
           tma_load_2d(sbase + Smem::b + s * kBChunkBytes, &tm_emb, (int)(kc * kBK),
-                      (int)(n * kBN), b_full(s));
+                      (int)(n * kBN + rank * kBNHalf), mapa(b_full(s), 0));
           issued[s] = issued[s] + 1u;
         }
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
-    if (lane == 0 && my_tiles > 0) {
+    // ---- MMA issuer (leader CTA only) ----
+    if (lane == 0 && my_tiles > 0 && leader) {
       bool ok = bar_wait(a_full, 0);
       uint32_t it = 0;
       for (uint32_t t = 0; ok && t < my_tiles && !*abort_flag; ++t) {
@@ -285,14 +329,14 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
           for (int k4 = 0; k4 < kBK / 16; ++k4)  // 16-element K steps inside the atom
             mma_f16(d, sw128_desc(a_addr + 32 * k4), sw128_desc(b_addr + 32 * k4),
                     (kc | (uint32_t)k4) != 0u);
-          mma_commit(b_empty(s));  // frees the stage once these MMAs have read it
+          mma_commit_pair(b_empty(s));  // frees the stage (both CTAs) once read
         }
         if (!ok) break;
-        mma_commit(acc_full(buf));
+        mma_commit_pair(acc_full(buf));
       }
       if (!ok) *abort_flag = 1u;
-      // all MMAs issued so far complete before TMEM is released
-      mma_commit(drain);
+      // all MMAs issued so far complete before either CTA releases TMEM
+      mma_commit_local(drain);
       bar_wait(drain, 0);
     }
   } else {
@@ -300,7 +344,9 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
     // (one hidden row per thread) and column half (w - 2) / 4 of each tile ----
     const uint32_t quad = (uint32_t)(warp & 3);
     const uint32_t half = (uint32_t)(warp - 2) >> 2;
-    const uint32_t row = m * kBM + quad * 32 + (uint32_t)lane;
+    const uint32_t row = m * 2 * kBM + rank * kBM + quad * 32 + (uint32_t)lane;
+    const uint32_t leader_acc_empty0 = mapa(acc_empty(0), 0);
+    const uint32_t leader_acc_empty1 = mapa(acc_empty(1), 0);
     const float qnan = __uint_as_float(0x7FC00000u);
     float best = __uint_as_float(0xFF800000u);  // -inf
     uint32_t best_col = 0xFFFFFFFFu;
@@ -337,7 +383,7 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(acc_empty(buf));
+      if (lane == 0) bar_arrive_cluster(buf ? leader_acc_empty1 : leader_acc_empty0);
     }
     if (my_tiles > 0 && row < p.rows && !*abort_flag) {
       // all-NaN (or empty) rows: NaN key of the shard's first id, which the
@@ -349,20 +395,27 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
     }
   }
 
-  // ---- teardown: drain the producer's copies, free TMEM ----
+  // ---- teardown: drain the producers' copies, free TMEM ----
   __syncthreads();
   if (*abort_flag && threadIdx.x == 0) {
-    // wait (bounded) for the last copy issued into each stage, and the hidden tile
     atomicOr(p.control + 1, 1u);
-    for (int s = 0; s < kStages; ++s)
-      if (issued[s] > 0u) bar_wait(b_full(s), (issued[s] - 1u) & 1u);
-    if (issued[kStages]) bar_wait(a_full, 0);
+    if (leader) {
+      // wait (bounded) for the last copy issued into each stage, and the hidden tile
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s] > 0u) bar_wait(b_full(s), (issued[s] - 1u) & 1u);
+      if (issued[kStages]) bar_wait(a_full, 0);
+    } else if (issued[kStages]) {
+      // the peer's copies complete on the leader's barriers: give any still
+      // in flight 1 ms (a copy of this GPU's memory takes microseconds)
+      const uint64_t t0 = global_ns();
+      while (global_ns() - t0 < 1000000ull) __nanosleep(10000);
+    }
   }
   fence_before();
-  __syncthreads();
+  cluster_sync();  // no CTA frees TMEM or exits while its pair may still touch it
   fence_after();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
                  : "memory");
 
@@ -452,6 +505,31 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t width,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Sets the kernel's shared-memory limit (once per device) and returns how
+// many CTA pairs can be resident at once: at most SMs / 2, fewer where a GPC
+// has an odd number of SMs free, so that the persistent grid is one wave.
+cudaError_t resident_pairs(int dev, int sms, uint32_t* pairs) {
+  static std::mutex mu;
+  static int cached[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  int& c = cached[dev & 63];
+  if (c == 0) {
+    cudaError_t e = cudaFuncSetAttribute(
+        dense_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(sms & ~1), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, dense_head_kernel, &cfg);
+    if (e != cudaSuccess) return e;
+    c = clusters < 1 ? 1 : (clusters > sms / 2 ? sms / 2 : clusters);
+  }
+  *pairs = (uint32_t)c;
+  return cudaSuccess;
+}
+
 }  // namespace
 
 extern "C" uint64_t mf_dense_workspace_bytes(uint64_t rows) { return ((rows * 8 + 16) + 15) & ~15ull; }
@@ -489,10 +567,13 @@ extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes
   p.k_chunks = (uint32_t)(hidden_size / kBK);
   p.vocab_rows = (uint32_t)vocab_rows;
   p.vocab_begin = (uint32_t)vocab_begin;
-  p.m_tiles = (uint32_t)((rows + kBM - 1) / kBM);
+  p.m_tiles = (uint32_t)((rows + 2 * kBM - 1) / (2 * kBM));
   p.n_tiles = (uint32_t)((vocab_rows + kBN - 1) / kBN);
-  if (p.m_tiles > (uint32_t)sms) return d_fail(MF_RESOURCE_LIMIT);  // rows <= 128 x SMs
-  p.per_m = (uint32_t)sms / p.m_tiles;
+  uint32_t pairs = 0;
+  e = resident_pairs(dev, sms, &pairs);
+  if (e != cudaSuccess) return d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+  if (p.m_tiles > pairs) return d_fail(MF_RESOURCE_LIMIT);  // rows <= 256 x SM pairs
+  p.per_m = pairs / p.m_tiles;
   if (p.per_m > p.n_tiles) p.per_m = p.n_tiles;
   char* ws = static_cast<char*>(workspace);
   p.keys = reinterpret_cast<unsigned long long*>(ws);
@@ -502,16 +583,10 @@ extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes
   p.out_scores = static_cast<float*>(out_scores);
   CUtensorMap tm_h, tm_e;
   if (!make_map(&tm_h, hidden, rows, hidden_size, kBM) ||
-      !make_map(&tm_e, embedding, vocab_rows, hidden_size, kBN))
+      !make_map(&tm_e, embedding, vocab_rows, hidden_size, kBNHalf))
     return d_fail(MF_CUDA_RUNTIME_FAILURE);
-  static bool attr_set[64] = {};
-  if (!attr_set[dev & 63]) {
-    e = cudaFuncSetAttribute(dense_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBytes);
-    if (e != cudaSuccess) return d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
-    attr_set[dev & 63] = true;
-  }
-  const unsigned grid = p.m_tiles * p.per_m;
+
+  const unsigned grid = 2 * p.m_tiles * p.per_m;  // CTA pairs (cluster dims 2)
   dense_head_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tm_h, tm_e,
                                                                                       p);
   e = cudaGetLastError();
@@ -535,7 +610,7 @@ extern "C" mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void*
 }
 
 // Self-test of the bounded waits (no counterpart in the reference): runs a
-// 128 x 256 x 64 dense problem whose producer issues no loads, so the MMA
+// 128 x 256 x 64 dense problem (one CTA pair) whose producers issue no loads, so the MMA
 // and epilogue waits run out (100 ms each).  The kernel must return, give
 // every row the sentinel and report the error word; the context stays
 // usable.  Allocates its small buffers with cudaMalloc and synchronises.
@@ -559,11 +634,11 @@ extern "C" mf_status mf_dense_selftest_wait_timeout(void* stream, uint32_t* erro
   if (e == cudaSuccess) e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   CUtensorMap tm_h, tm_e;
-  if (e == cudaSuccess && (!make_map(&tm_h, hid, rows, hs, kBM) || !make_map(&tm_e, emb, vocab, hs, kBN)))
+  if (e == cudaSuccess &&
+      (!make_map(&tm_h, hid, rows, hs, kBM) || !make_map(&tm_e, emb, vocab, hs, kBNHalf)))
     st = d_fail(MF_CUDA_RUNTIME_FAILURE);
-  if (e == cudaSuccess && st.code == MF_OK)
-    e = cudaFuncSetAttribute(dense_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBytes);
+  uint32_t pairs = 0;
+  if (e == cudaSuccess && st.code == MF_OK) e = resident_pairs(dev, sms, &pairs);
   if (e == cudaSuccess && st.code == MF_OK) {
     Params p{};
     p.rows = (uint32_t)rows;
@@ -577,7 +652,7 @@ extern "C" mf_status mf_dense_selftest_wait_timeout(void* stream, uint32_t* erro
     p.out_ids = static_cast<uint32_t*>(ids);
     p.error_out = static_cast<uint32_t*>(err);
     p.skip_loads = 1u;
-    dense_head_kernel<<<1, kThreads, kSmemBytes, s>>>(tm_h, tm_e, p);
+    dense_head_kernel<<<2, kThreads, kSmemBytes, s>>>(tm_h, tm_e, p);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   }
