@@ -338,8 +338,10 @@ DENSE_STEPS = 200
 def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ranks):
     """Config 4: B = 1024 RMSNorm'd hidden rows x the full 49,152-row vocabulary,
     FP32 accumulate, fused argmax.  Under torchrun the vocabulary is sharded
-    (49,152 / N rows per GPU, the tcgen05 kernel over each shard) and the
-    packed keys merge with one NCCL max all-reduce of B x 8 bytes."""
+    (49,152 / N rows per GPU) and the shards merge inside the tcgen05 kernel
+    (``dense_head_sharded_f16``: keys exchanged over NVLink through CUDA IPC
+    buffers); the same step with a NCCL max all-reduce of the keys and a
+    decode launch is timed beside it for comparison."""
     import torch
     import torch.distributed as dist
 
@@ -355,55 +357,73 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
     ws = torch.zeros(head.dense_workspace_bytes(DENSE_ROWS), dtype=torch.uint8, device=device)
     flip = head.KEY_SIGN_FLIP - 2**64
     h = stream.cuda_stream
+    ex = head.VocabShardExchange(DENSE_ROWS) if world > 1 else None
 
     def step(i):
+        if world > 1:
+            st = head.dense_head_sharded_f16(hid, shards[i % len(shards)], None, ids, None, ws,
+                                             DENSE_ROWS, 576, per, v0, ex, h)
+        else:
+            st = head.dense_head_f16(hid, shards[i % len(shards)], None, ids, None, ws,
+                                     DENSE_ROWS, 576, per, v0, h)
+        if not st.ok():
+            raise RuntimeError(f"dense head failed: {st}")
+
+    def step_nccl(i):
         st = head.dense_head_f16(hid, shards[i % len(shards)], keys, None, None, ws, DENSE_ROWS,
                                  576, per, v0, h)
         if not st.ok():
             raise RuntimeError(f"dense head failed: {st}")
-        if world > 1:
-            keys.bitwise_xor_(flip)
-            dist.all_reduce(keys, op=dist.ReduceOp.MAX)
-            keys.bitwise_xor_(flip)
+        keys.bitwise_xor_(flip)
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+        keys.bitwise_xor_(flip)
         st = head.decode_keys(keys, ids, None, DENSE_ROWS, h)
         if not st.ok():
             raise RuntimeError(f"decode failed: {st}")
 
-    with torch.cuda.stream(stream):
-        for i in range(5):
-            step(i)
-    stream.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        t0.record(stream)
-        for i in range(DENSE_STEPS):
-            step(i)
-        t1.record(stream)
-        # the GEMM kernel alone, for the tensor-core roofline
-        k0.record(stream)
-        for i in range(DENSE_STEPS):
-            head.dense_head_f16(hid, shards[i % len(shards)], keys, None, None, ws, DENSE_ROWS, 576,
-                                per, v0, h)
-        k1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    ms = max_over_ranks(t0.elapsed_time(t1)) / DENSE_STEPS
-    kms = max_over_ranks(k0.elapsed_time(k1)) / DENSE_STEPS
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            for i in range(5):
+                fn(i)
+        stream.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            t0.record(stream)
+            for i in range(DENSE_STEPS):
+                fn(i)
+            t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(t0.elapsed_time(t1)) / DENSE_STEPS
+
+    ms = timed(step)
+    nccl_ms = timed(step_nccl) if world > 1 else None
+
+    def kernel_only(i):
+        head.dense_head_f16(hid, shards[i % len(shards)], keys, None, None, ws, DENSE_ROWS, 576,
+                            per, v0, h)
+
+    kms = timed(kernel_only)  # the GEMM kernel alone, for the tensor-core roofline
+    if ex is not None:
+        ex.close()
     flop = 2.0 * DENSE_ROWS * vocab * 576
     peak = _tensor_peak()
     per_gpu_tflops = 2.0 * DENSE_ROWS * per * 576 / (kms * 1e-3) / 1e12
-    return {"workload": f"B={DENSE_ROWS} x V={vocab} x 576 fp16, f32 accumulate, fused argmax, "
-                        f"vocab-sharded {per} rows/GPU" + (", NCCL max all-reduce of keys" if world > 1 else ""),
-            "seq_per_s": DENSE_ROWS / (ms * 1e-3), "ms_per_step": ms,
-            "tflops_job": flop / (ms * 1e-3) / 1e12,
-            "kernel_us": kms * 1e3,
-            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peak[0],
-                         "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1],
-                         "traffic": TRAFFIC_DENSE if world == 1 else None},
-            "steps": DENSE_STEPS}
+    out = {"workload": f"B={DENSE_ROWS} x V={vocab} x 576 fp16, f32 accumulate, fused argmax, "
+                       f"vocab-sharded {per} rows/GPU"
+                       + (", shards merged in-kernel over NVLink" if world > 1 else ""),
+           "seq_per_s": DENSE_ROWS / (ms * 1e-3), "ms_per_step": ms,
+           "tflops_job": flop / (ms * 1e-3) / 1e12,
+           "kernel_us": kms * 1e3,
+           "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peak[0],
+                        "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1],
+                        "traffic": TRAFFIC_DENSE if world == 1 else None},
+           "steps": DENSE_STEPS}
+    if nccl_ms is not None:
+        out["nccl_merge_ms_per_step"] = nccl_ms
+    return out
 
 
 K_SWEEP = (1, 8, 64, 512, 4096, 49_152)

@@ -193,7 +193,7 @@ MF_API mf_status mf_dfa_decode_f16(const void* hidden, uint64_t hidden_bytes,
  * the tensor cores and keeps only each row's best (score, id).  hidden: fp16
  * [rows, hidden_size]; embedding: fp16 [vocab_rows, hidden_size], the rows
  * of vocabulary ids [vocab_begin, vocab_begin + vocab_rows).  hidden_size is
- * a multiple of 64 up to 576; rows <= 128 x SM count.  Outputs (either may
+ * a multiple of 64 up to 576; rows <= 256 x (SM pairs that can be co-resident).  Outputs (either may
  * be NULL, not both): out_keys u64 [rows] — the packed key whose unsigned
  * max over shards is the global selection (so vocabulary shards on several
  * GPUs merge with one max all-reduce, then mf_decode_keys) — and out_ids u32
@@ -217,6 +217,36 @@ MF_API mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes,
 MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out_ids,
                                 uint64_t out_ids_bytes, void* out_scores,
                                 uint64_t out_scores_bytes, uint64_t rows, void* stream);
+
+/* ---- vocabulary shards on several GPUs, merged inside the dense kernel ----
+ *
+ * Replaces "mf_dense_head_f16 per shard + max all-reduce of the keys +
+ * mf_decode_keys" (the reference's single-GPU linear_f16 + greedy_select_f16,
+ * src/cuda/linear.cu:40-104 and src/cuda/greedy.cu:237-279, split by vocab
+ * rows) with one launch per rank: the kernel's last CTA stores its keys into
+ * every rank's exchange buffer over NVLink, waits (bounded, 100 ms) for every
+ * rank's keys, and writes the global ids/scores (and merged keys) on every
+ * rank.  One process per GPU, one exchange buffer per rank:
+ *   mf_exchange_alloc      cudaMalloc + zero + cudaIpcGetMemHandle (64-byte handle)
+ *   (the caller all-gathers the handles, e.g. over torch.distributed)
+ *   mf_exchange_open_peer  cudaIpcOpenMemHandle of a peer's handle
+ * exchange[q] is rank q's buffer as mapped in this process (the own buffer
+ * at exchange[rank]); world <= 8; every rank calls with the same rows, in
+ * the same order, on its own GPU.  A rank whose peers do not arrive within
+ * 100 ms gives every row the sentinel; the context stays usable. */
+#define MF_IPC_HANDLE_BYTES 64
+MF_API uint64_t mf_exchange_bytes(uint64_t rows, uint32_t world);
+MF_API mf_status mf_exchange_alloc(void** buffer, uint64_t bytes, void* ipc_handle);
+MF_API mf_status mf_exchange_free(void* buffer);
+MF_API mf_status mf_exchange_open_peer(const void* ipc_handle, void** peer_buffer);
+MF_API mf_status mf_exchange_close_peer(void* peer_buffer);
+MF_API mf_status mf_dense_head_sharded_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    void* out_keys, uint64_t out_keys_bytes, void* out_ids, uint64_t out_ids_bytes,
+    void* out_scores, uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes,
+    uint64_t rows, uint64_t hidden_size, uint64_t vocab_rows, uint64_t vocab_begin,
+    void* const* exchange, uint64_t exchange_bytes, uint32_t world, uint32_t rank,
+    void* stream);
 
 /* Self-test of the dense kernel's bounded waits (no counterpart in the
  * reference): a tiny dense problem whose loads are never issued, so its

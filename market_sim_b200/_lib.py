@@ -47,6 +47,12 @@ _SIGNATURES["mf_dense_head_f16"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, 
 _SIGNATURES["mf_dense_selftest_wait_timeout"] = [_P, ctypes.POINTER(ctypes.c_uint32),
                                                  ctypes.POINTER(ctypes.c_uint32)]
 _SIGNATURES["mf_decode_keys"] = [_P, _U64, _P, _U64, _P, _U64, _U64, _P]
+_SIGNATURES["mf_exchange_alloc"] = [ctypes.POINTER(_P), _U64, _P]
+_SIGNATURES["mf_exchange_free"] = [_P]
+_SIGNATURES["mf_exchange_open_peer"] = [_P, ctypes.POINTER(_P)]
+_SIGNATURES["mf_exchange_close_peer"] = [_P]
+_SIGNATURES["mf_dense_head_sharded_f16"] = ([_P, _U64] * 6 + [_U64] * 4
+                                            + [_P, _U64, ctypes.c_uint32, ctypes.c_uint32, _P])
 
 _SIGNATURES["mf_pipeline_create"] = [ctypes.POINTER(_P), _P, _U64, _U64, _U64, _U64, _U64,
                                      ctypes.c_uint32]
@@ -56,7 +62,7 @@ _SIGNATURES["mf_pipeline_wait"] = [_P, _U64]
 _SIGNATURES["mf_pipeline_synchronize"] = [_P]
 
 _U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64],
-              "mf_dense_workspace_bytes": [_U64]}
+              "mf_dense_workspace_bytes": [_U64], "mf_exchange_bytes": [_U64, ctypes.c_uint32]}
 _U32_FUNCS = {"mf_version": [], "mf_built_arch": []}
 _PTR_FUNCS = {"mf_pipeline_stream": [_P, ctypes.c_uint32]}
 _VOID_FUNCS = {"mf_pipeline_destroy": [_P]}

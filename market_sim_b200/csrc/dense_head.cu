@@ -34,6 +34,17 @@
 // order is the selection rule (see common.cuh), so vocabulary shards on
 // several GPUs merge with a plain max-reduction of the keys.
 //
+// Vocabulary shards on several GPUs (mf_dense_head_sharded_f16): the merge
+// is fused into the same kernel.  The last CTA on each rank stores its keys
+// into every rank's exchange buffer over NVLink (plain peer stores through
+// CUDA IPC mappings), raises its epoch flag there with a system-scope
+// release, waits (bounded) for every rank's flag in its own buffer, and
+// decodes the maximum.  This replaces a NCCL max all-reduce of the keys and
+// the decode launch.  Exchange buffer of one rank (mf_exchange_bytes):
+//   u32 epoch (this rank's call counter) at 0, u32 flags[world] at 64,
+//   u64 slots[2][world][rows] at 512, parity = epoch & 1, so a rank one call
+//   ahead never overwrites keys a slower rank is still reading.
+//
 // Every mbarrier wait is bounded; a wait that runs out sets an abort flag
 // and the error word in the workspace, and the CTA drains its in-flight
 // copies and MMAs (bounded again) before freeing TMEM and exiting.
@@ -41,6 +52,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <initializer_list>
 #include <mutex>
 
@@ -61,6 +73,9 @@ constexpr int kEpiWarps = 8;      // two per TMEM lane quadrant, each on half th
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA, epilogue warps
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 100ull * 1000 * 1000;  // 100 ms per mbarrier wait
+constexpr int kMaxRanks = 8;       // GPUs of one node
+constexpr int kXFlags = 64;        // exchange buffer: flags offset
+constexpr int kXSlots = 512;       // exchange buffer: slots offset
 
 struct Smem {  // offsets inside the 1024-aligned dynamic shared memory
   static constexpr int a = 0;
@@ -89,6 +104,8 @@ struct Params {
   float* out_scores;
   uint32_t* error_out;       // optional: receives the error word (self-test)
   uint32_t skip_loads;       // self-test only: the producer issues nothing
+  uint32_t world, rank;      // vocabulary shards merged in-kernel when world > 1
+  unsigned char* xbuf[kMaxRanks];  // every rank's exchange buffer, as mapped here
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -427,14 +444,75 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
   if (s_last) {
     __threadfence();
     const bool failed = atomicAdd(p.control + 1, 0u) != 0u;
-    if (threadIdx.x == 0 && p.error_out) *p.error_out = failed ? 1u : 0u;
-    for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
-      const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
-      if (failed) p.keys[r] = 0ull;
-      if (p.out_keys) p.out_keys[r] = key;
-      if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
-      if (p.out_scores)
-        p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+    if (p.world > 1) {
+      // ---- fused vocabulary-shard merge over the exchange buffers ----
+      __shared__ uint32_t s_epoch, s_xfail;
+      unsigned char* self = p.xbuf[p.rank];
+      if (threadIdx.x == 0) {
+        s_epoch = *reinterpret_cast<volatile uint32_t*>(self) + 1u;
+        s_xfail = 0u;
+      }
+      __syncthreads();
+      const uint32_t epoch = s_epoch;
+      const size_t par_off = kXSlots + (size_t)(epoch & 1u) * p.world * p.rows * 8;
+      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+        const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
+        if (failed) p.keys[r] = 0ull;
+        for (uint32_t q = 0; q < p.world; ++q)
+          reinterpret_cast<unsigned long long*>(p.xbuf[q] + par_off)[(size_t)p.rank * p.rows + r] = key;
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x < p.world) {
+        uint32_t* flag = reinterpret_cast<uint32_t*>(p.xbuf[threadIdx.x] + kXFlags) + p.rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+      }
+      if (threadIdx.x < p.world) {
+        // wait (bounded) until rank threadIdx.x has stored this call's keys here
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(self + kXFlags) + threadIdx.x;
+        const uint64_t start = global_ns();
+        for (uint32_t i = 0;; ++i) {
+          uint32_t v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+          if ((int32_t)(v - epoch) >= 0) break;
+          if ((i & 63u) == 63u && global_ns() - start > kWaitLimitNs) {
+            atomicOr(&s_xfail, 1u);
+            break;
+          }
+        }
+      }
+      __syncthreads();
+      const bool xfail = failed || s_xfail != 0u;
+      if (threadIdx.x == 0 && p.error_out) *p.error_out = xfail ? 1u : 0u;
+      const unsigned long long* slots =
+          reinterpret_cast<const unsigned long long*>(self + par_off);
+      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+        unsigned long long key = 0ull;
+        for (uint32_t q = 0; q < p.world; ++q) {
+          unsigned long long k;
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
+                       : "=l"(k)
+                       : "l"(slots + (size_t)q * p.rows + r)
+                       : "memory");
+          key = k > key ? k : key;
+        }
+        if (xfail) key = kKeyPoison;
+        if (p.out_keys) p.out_keys[r] = key;
+        if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
+        if (p.out_scores)
+          p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+      }
+      if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(self) = epoch;
+    } else {
+      if (threadIdx.x == 0 && p.error_out) *p.error_out = failed ? 1u : 0u;
+      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+        const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
+        if (failed) p.keys[r] = 0ull;
+        if (p.out_keys) p.out_keys[r] = key;
+        if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
+        if (p.out_scores)
+          p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+      }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -534,14 +612,17 @@ cudaError_t resident_pairs(int dev, int sms, uint32_t* pairs) {
 
 extern "C" uint64_t mf_dense_workspace_bytes(uint64_t rows) { return ((rows * 8 + 16) + 15) & ~15ull; }
 
-extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes,
-                                       const void* embedding, uint64_t embedding_bytes,
-                                       void* out_keys, uint64_t out_keys_bytes, void* out_ids,
-                                       uint64_t out_ids_bytes, void* out_scores,
-                                       uint64_t out_scores_bytes, void* workspace,
-                                       uint64_t workspace_bytes, uint64_t rows,
-                                       uint64_t hidden_size, uint64_t vocab_rows,
-                                       uint64_t vocab_begin, void* stream) {
+namespace {
+
+// Validates and launches the dense head; world > 1 merges the vocabulary
+// shards in-kernel through the exchange buffers `xbuf` (already checked).
+mf_status dense_launch(const void* hidden, uint64_t hidden_bytes, const void* embedding,
+                       uint64_t embedding_bytes, void* out_keys, uint64_t out_keys_bytes,
+                       void* out_ids, uint64_t out_ids_bytes, void* out_scores,
+                       uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes,
+                       uint64_t rows, uint64_t hidden_size, uint64_t vocab_rows,
+                       uint64_t vocab_begin, uint32_t world, uint32_t rank,
+                       unsigned char* const* xbuf, void* stream) {
   if (rows == 0 || hidden_size == 0 || vocab_rows == 0 || stream == nullptr)
     return d_fail(MF_INVALID_ARGUMENT);
   if (hidden_size % kBK != 0 || hidden_size > (uint64_t)kMaxKChunks * kBK)
@@ -581,6 +662,10 @@ extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes
   p.out_keys = static_cast<unsigned long long*>(out_keys);
   p.out_ids = static_cast<uint32_t*>(out_ids);
   p.out_scores = static_cast<float*>(out_scores);
+  p.world = world;
+  p.rank = rank;
+  if (world > 1)  // the caller checked world <= kMaxRanks and every pointer
+    for (uint32_t q = 0; q < world; ++q) p.xbuf[q] = xbuf[q];
   CUtensorMap tm_h, tm_e;
   if (!make_map(&tm_h, hidden, rows, hidden_size, kBM) ||
       !make_map(&tm_e, embedding, vocab_rows, hidden_size, kBNHalf))
@@ -591,6 +676,87 @@ extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes
                                                                                       p);
   e = cudaGetLastError();
   return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_BACKEND_FAILURE, (uint32_t)e);
+}
+
+}  // namespace
+
+extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes,
+                                       const void* embedding, uint64_t embedding_bytes,
+                                       void* out_keys, uint64_t out_keys_bytes, void* out_ids,
+                                       uint64_t out_ids_bytes, void* out_scores,
+                                       uint64_t out_scores_bytes, void* workspace,
+                                       uint64_t workspace_bytes, uint64_t rows,
+                                       uint64_t hidden_size, uint64_t vocab_rows,
+                                       uint64_t vocab_begin, void* stream) {
+  return dense_launch(hidden, hidden_bytes, embedding, embedding_bytes, out_keys,
+                      out_keys_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes,
+                      workspace, workspace_bytes, rows, hidden_size, vocab_rows, vocab_begin, 1u,
+                      0u, nullptr, stream);
+}
+
+extern "C" uint64_t mf_exchange_bytes(uint64_t rows, uint32_t world) {
+  return (uint64_t)kXSlots + 2ull * world * rows * 8ull;
+}
+
+extern "C" mf_status mf_exchange_alloc(void** buffer, uint64_t bytes, void* ipc_handle) {
+  if (buffer == nullptr || ipc_handle == nullptr || bytes < (uint64_t)kXSlots)
+    return d_fail(MF_INVALID_ARGUMENT);
+  *buffer = nullptr;
+  void* b = nullptr;
+  cudaError_t e = cudaMalloc(&b, bytes);
+  if (e == cudaSuccess) e = cudaMemset(b, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, b);
+  if (e != cudaSuccess) {
+    cudaFree(b);
+    return d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+  }
+  static_assert(sizeof(h) == MF_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *buffer = b;
+  return d_ok();
+}
+
+extern "C" mf_status mf_exchange_free(void* buffer) {
+  const cudaError_t e = cudaFree(buffer);
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+}
+
+extern "C" mf_status mf_exchange_open_peer(const void* ipc_handle, void** peer_buffer) {
+  if (ipc_handle == nullptr || peer_buffer == nullptr) return d_fail(MF_INVALID_ARGUMENT);
+  *peer_buffer = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+}
+
+extern "C" mf_status mf_exchange_close_peer(void* peer_buffer) {
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_buffer);
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+}
+
+extern "C" mf_status mf_dense_head_sharded_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    void* out_keys, uint64_t out_keys_bytes, void* out_ids, uint64_t out_ids_bytes,
+    void* out_scores, uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes,
+    uint64_t rows, uint64_t hidden_size, uint64_t vocab_rows, uint64_t vocab_begin,
+    void* const* exchange, uint64_t exchange_bytes, uint32_t world, uint32_t rank,
+    void* stream) {
+  if (world == 0 || rank >= world || exchange == nullptr) return d_fail(MF_INVALID_ARGUMENT);
+  if (world > (uint32_t)kMaxRanks) return d_fail(MF_RESOURCE_LIMIT);
+  if (exchange_bytes < mf_exchange_bytes(rows, world)) return d_fail(MF_INVALID_ARGUMENT);
+  unsigned char* xbuf[kMaxRanks] = {};
+  for (uint32_t q = 0; q < world; ++q) {
+    xbuf[q] = static_cast<unsigned char*>(exchange[q]);
+    if (xbuf[q] == nullptr || (uintptr_t)xbuf[q] % 256 != 0) return d_fail(MF_INVALID_ARGUMENT);
+    for (uint32_t j = 0; j < q; ++j)
+      if (xbuf[j] == xbuf[q]) return d_fail(MF_INVALID_ARGUMENT);
+  }
+  return dense_launch(hidden, hidden_bytes, embedding, embedding_bytes, out_keys,
+                      out_keys_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes,
+                      workspace, workspace_bytes, rows, hidden_size, vocab_rows, vocab_begin,
+                      world, rank, xbuf, stream);
 }
 
 extern "C" mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out_ids,

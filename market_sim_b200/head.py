@@ -329,6 +329,93 @@ def decode_keys(keys: Buffer, token_ids: Buffer, scores: Optional[Buffer], rows:
                                       _sp(stream)))
 
 
+IPC_HANDLE_BYTES = 64
+
+
+def exchange_bytes(rows: int, world: int) -> int:
+    """Bytes of one rank's exchange buffer for ``dense_head_sharded_f16``."""
+    return int(lib.mf_exchange_bytes(rows, world))
+
+
+def dense_head_sharded_f16(hidden: Buffer, embedding: Buffer, keys: Optional[Buffer],
+                           token_ids: Optional[Buffer], scores: Optional[Buffer],
+                           workspace: Buffer, rows: int, hidden_size: int, vocab_rows: int,
+                           vocab_begin: int, exchange, stream) -> Status:
+    """Vocabulary shards on several GPUs merged inside the dense kernel: every
+    rank calls this on its own shard (``vocab_begin`` = the shard's first id)
+    and gets the global ids / scores / keys.  ``exchange`` is a
+    ``VocabShardExchange`` (or any object with ``ptrs``, ``nbytes``,
+    ``world`` and ``rank``)."""
+    arr = (ctypes.c_void_p * len(exchange.ptrs))(*exchange.ptrs)
+    return _status(lib.mf_dense_head_sharded_f16(
+        *_pb(hidden), *_pb(embedding), *_pb(keys), *_pb(token_ids), *_pb(scores),
+        *_pb(workspace), rows, hidden_size, vocab_rows, vocab_begin, arr, exchange.nbytes,
+        exchange.world, exchange.rank, _sp(stream)))
+
+
+class VocabShardExchange:
+    """The exchange buffers of ``dense_head_sharded_f16``: this rank allocates
+    its own (``mf_exchange_alloc``), the 64-byte CUDA IPC handles are
+    all-gathered (``all_gather(bytes) -> list[bytes]``, by default
+    ``torch.distributed.all_gather_object`` on ``group``) and every peer's
+    buffer is mapped here (``mf_exchange_open_peer``).  One process per GPU;
+    the current device must be this rank's GPU."""
+
+    def __init__(self, rows: int, world: int = None, rank: int = None, group=None,
+                 all_gather=None):
+        if world is None or rank is None:
+            import torch.distributed as dist
+
+            world, rank = dist.get_world_size(group), dist.get_rank(group)
+        if all_gather is None:
+            import torch.distributed as dist
+
+            def all_gather(b: bytes):
+                out = [None] * world
+                dist.all_gather_object(out, b, group=group)
+                return out
+        self.world, self.rank, self.rows = int(world), int(rank), int(rows)
+        self.nbytes = exchange_bytes(rows, world)
+        own, handle = ctypes.c_void_p(), ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        st = _status(lib.mf_exchange_alloc(ctypes.byref(own), self.nbytes, handle))
+        if not st.ok():
+            raise RuntimeError(f"mf_exchange_alloc failed: {st}")
+        self._own = own.value
+        self._opened = []
+        handles = all_gather(handle.raw)
+        ptrs = []
+        try:
+            for q, h in enumerate(handles):
+                if q == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                st = _status(lib.mf_exchange_open_peer(ctypes.create_string_buffer(h, len(h)),
+                                                       ctypes.byref(peer)))
+                if not st.ok():
+                    raise RuntimeError(f"mf_exchange_open_peer({q}) failed: {st}")
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+        except Exception:
+            self.close()
+            raise
+        self.ptrs = ptrs
+
+    def close(self) -> None:
+        for p in self._opened:
+            lib.mf_exchange_close_peer(p)
+        self._opened = []
+        if self._own:
+            lib.mf_exchange_free(self._own)
+            self._own = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 KEY_SIGN_FLIP = 1 << 63
 """XOR with this maps the unsigned key order onto signed int64 order, so a
 signed MAX all-reduce (NCCL / torch.distributed) merges keys correctly."""

@@ -161,3 +161,113 @@ def test_dense_bounded_waits_give_up_cleanly(mf):
     _, ids, _ = _dense(mf, to_dev(h), to_dev(e), 64, 576, 300)
     assert (ids < 300).all()
     torch.cuda.synchronize()
+
+
+class _Exchange:
+    """Exchange buffers given as raw pointers (both on this GPU)."""
+
+    def __init__(self, ptrs, nbytes, world, rank):
+        self.ptrs, self.nbytes, self.world, self.rank = ptrs, nbytes, world, rank
+
+
+def _slot(buf, rows, world, epoch, q):
+    """Rank q's keys for call `epoch` inside one exchange buffer (u64 view)."""
+    par = epoch & 1
+    off = 512 + (par * world + q) * rows * 8
+    return buf[off:off + rows * 8].view(dtype=__import__("torch").int64)
+
+
+def _flag(buf, q):
+    import torch
+
+    return buf[64 + 4 * q:64 + 4 * q + 4].view(torch.int32)
+
+
+def test_dense_sharded_merge_emulated_peer(mf):
+    """In-kernel vocabulary-shard merge on one GPU: rank 1's keys and flag
+    are stored into rank 0's exchange buffer beforehand (as rank 1 would over
+    NVLink), so rank 0's kernel never waits on another launch.  Over three
+    calls (epochs 1-3, both slot parities) rank 0's ids / scores / keys equal
+    the unsharded head, and rank 0's keys and flag land in the peer buffer."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    rows, vocab, hs, world = 256, 8192, 576, 2
+    per = vocab // world
+    e = synth.embedding(91, vocab=vocab)
+    h = synth.hidden_states(92, rows)
+    e_d, h_d = to_dev(e), to_dev(h)
+    full_keys, full_ids, full_sc = _dense(mf, h_d, e_d, rows, hs, vocab)
+    k0, _, _ = _dense(mf, h_d, e_d[:per].contiguous(), rows, hs, per, 0)
+    k1, _, _ = _dense(mf, h_d, e_d[per:].contiguous(), rows, hs, per, per)
+    nbytes = mf.exchange_bytes(rows, world)
+    own = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    peer = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ex = _Exchange([own.data_ptr(), peer.data_ptr()], nbytes, world, 0)
+    shard0 = e_d[:per].contiguous()
+    ws = torch.zeros(mf.dense_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    for epoch in (1, 2, 3):
+        _slot(own, rows, world, epoch, 1).copy_(torch.from_numpy(k1.view(np.int64)))
+        _flag(own, 1).fill_(epoch)
+        keys = torch.empty(rows, dtype=torch.int64, device="cuda")
+        ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+        sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+        st = mf.dense_head_sharded_f16(h_d, shard0, keys, ids, sc, ws, rows, hs, per, 0, ex,
+                                       gpu_stream())
+        assert st.ok(), st
+        torch.cuda.synchronize()
+        assert np.array_equal(keys.cpu().numpy().view(np.uint64), full_keys)
+        assert np.array_equal(ids.cpu().numpy().view(np.uint32), full_ids)
+        assert np.array_equal(sc.cpu().numpy().view(np.uint32), full_sc.view(np.uint32))
+        assert np.array_equal(_slot(peer, rows, world, epoch, 0).cpu().numpy().view(np.uint64), k0)
+        assert int(_flag(peer, 0).item()) == epoch
+        assert int(own[:4].view(torch.int32).item()) == epoch
+        assert int(ws.sum()) == 0
+
+
+def test_dense_sharded_peer_never_arrives(mf):
+    """A peer that never stores its keys: the wait runs out after 100 ms, the
+    rows get the sentinel on this rank, and the context stays usable."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    rows, vocab, hs, world = 128, 1024, 576, 2
+    e_d = to_dev(synth.embedding(93, vocab=vocab))
+    h_d = to_dev(synth.hidden_states(94, rows))
+    nbytes = mf.exchange_bytes(rows, world)
+    own = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    peer = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ex = _Exchange([own.data_ptr(), peer.data_ptr()], nbytes, world, 0)
+    ids = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(mf.dense_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    st = mf.dense_head_sharded_f16(h_d, e_d, None, ids, None, ws, rows, hs, vocab, 0, ex,
+                                   gpu_stream())
+    assert st.ok(), st
+    torch.cuda.synchronize()
+    assert (ids.cpu().numpy().view(np.uint32) == INVALID).all()
+    assert int(ws.sum()) == 0
+    _, ids2, _ = _dense(mf, h_d, e_d, rows, hs, vocab)
+    assert (ids2 < vocab).all()
+
+
+def test_dense_sharded_rejects(mf):
+    import torch
+
+    E = mf.ErrorCode
+    rows, hs, vocab = 128, 64, 256
+    h = torch.zeros((rows, hs), dtype=torch.float16, device="cuda")
+    e = torch.zeros((vocab, hs), dtype=torch.float16, device="cuda")
+    ids = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(mf.dense_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    nb = mf.exchange_bytes(rows, 2)
+    a = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    b = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    s = gpu_stream()
+    call = lambda ex: mf.dense_head_sharded_f16(h, e, None, ids, None, ws, rows, hs, vocab, 0, ex, s)
+    assert call(_Exchange([a.data_ptr(), b.data_ptr()], nb, 2, 2)).code == E.invalid_argument
+    assert call(_Exchange([a.data_ptr(), a.data_ptr()], nb, 2, 0)).code == E.invalid_argument
+    assert call(_Exchange([a.data_ptr(), b.data_ptr()], nb - 8, 2, 0)).code == E.invalid_argument
+    assert call(_Exchange([a.data_ptr(), b.data_ptr() + 8], nb, 2, 0)).code == E.invalid_argument
+    assert call(_Exchange([a.data_ptr()] * 9, nb, 9, 0)).code == E.resource_limit
