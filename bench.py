@@ -381,31 +381,45 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
         if not st.ok():
             raise RuntimeError(f"decode failed: {st}")
 
-    def timed(fn):
+    def timed(fn, graph):
+        """Per-step ms over DENSE_STEPS steps (max over ranks); graph=True
+        captures the steps in one CUDA graph and times a replay."""
         with torch.cuda.stream(stream):
             for i in range(5):
                 fn(i)
         stream.synchronize()
+        g = None
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(DENSE_STEPS):
+                    fn(i)
+            g.replay()
+            stream.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             t0.record(stream)
-            for i in range(DENSE_STEPS):
-                fn(i)
+            if g is not None:
+                g.replay()
+            else:
+                for i in range(DENSE_STEPS):
+                    fn(i)
             t1.record(stream)
         torch.cuda.synchronize()
         barrier()
         return max_over_ranks(t0.elapsed_time(t1)) / DENSE_STEPS
 
-    ms = timed(step)
-    nccl_ms = timed(step_nccl) if world > 1 else None
+    ms = timed(step, True)
+    eager_ms = timed(step, False)
+    nccl_ms = timed(step_nccl, False) if world > 1 else None
 
     def kernel_only(i):
         head.dense_head_f16(hid, shards[i % len(shards)], keys, None, None, ws, DENSE_ROWS, 576,
                             per, v0, h)
 
-    kms = timed(kernel_only)  # the GEMM kernel alone, for the tensor-core roofline
+    kms = timed(kernel_only, True)  # the GEMM kernel alone, for the tensor-core roofline
     if ex is not None:
         ex.close()
     flop = 2.0 * DENSE_ROWS * vocab * 576
@@ -420,7 +434,12 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peak[0],
                         "unit": "TFLOP/s", "frac": per_gpu_tflops / peak[0], "peak_kind": peak[1],
                         "traffic": TRAFFIC_DENSE if world == 1 else None},
-           "steps": DENSE_STEPS}
+           "steps": DENSE_STEPS,
+           "timing": "steps and kernel_us: one CUDA graph of the steps, events around a replay; "
+                     "eager_ms_per_step: the same steps launched from Python"
+                     + ("; nccl_merge_ms_per_step: kernel + sign flip + NCCL max all-reduce + "
+                        "decode, launched from Python" if world > 1 else ""),
+           "eager_ms_per_step": eager_ms}
     if nccl_ms is not None:
         out["nccl_merge_ms_per_step"] = nccl_ms
     return out
