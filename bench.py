@@ -37,7 +37,7 @@ sys.path.insert(0, ROOT)
 METRIC = "restricted-head seq/s & achieved HBM GB/s (vs ~8 TB/s), B=256 ragged, 1-8 GPUs"
 UNIT = "seq/s"
 ROWS = 256
-PIPE_DEPTH = 6  # host pipeline slots in flight for the e2e leg (2: 6.1, 4: 7.8, 6: 8.3 M seq/s measured)
+PIPE_DEPTH = 6  # host pipeline slots in flight for the e2e leg (4: 11.9, 6: 12.6, 8: 12.7 M seq/s measured)
 KMAX = 4096
 REPLICAS = 6
 BATCHES = 8
@@ -173,11 +173,12 @@ def run_ours(args):
     ws = torch.zeros(head.head_workspace_bytes(ROWS), dtype=torch.uint8, device=device)
     h = stream.cuda_stream
 
-    def step(i):
+    def step(i, flags=0):
         b = batches[i % BATCHES]
         e = replicas[i % REPLICAS]
-        st = head.restricted_output_head_csr_f16(b["hid_d"], e, b["off_d"], b["ids_d"], out_ids,
-                                                 out_sc, ws, ROWS, 576, 49_152, h)
+        st = head.restricted_output_head_csr_f16_ex(b["hid_d"], e, b["off_d"], b["ids_d"],
+                                                    out_ids, out_sc, ws, ROWS, 576, 49_152, flags,
+                                                    h)
         if not st.ok():
             raise RuntimeError(f"head failed: {st}")
 
@@ -206,7 +207,9 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         with torch.cuda.graph(graph, stream=stream):
             for i in range(args.steps):
-                step(args.warmup + i)
+                # consecutive batches are independent: each launch may start
+                # while the previous one drains (programmatic dependent launch)
+                step(args.warmup + i, head.LAUNCH_OVERLAP_PREVIOUS)
         graph.replay()  # untimed warm replay
     stream.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -269,12 +272,22 @@ def run_ours(args):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    s_in = torch.cuda.ExternalStream(pipe.stream(0), device=device)
-    s_out = torch.cuda.ExternalStream(pipe.stream(2), device=device)
-    e0.record(s_in)
+    slot_streams = [torch.cuda.ExternalStream(pipe.stream(k), device=device)
+                    for k in range(pipe.depth())]
+    # e0 on slot 0's stream, which every other slot stream waits for; at the
+    # end slot 0's stream waits for every other slot, then e1
+    e0.record(slot_streams[0])
+    for st_ in slot_streams[1:]:
+        st_.wait_event(e0)
+    host_t0 = time.perf_counter()
     for i in range(args.steps):
         e2e_step(args.warmup + i, True)
-    e1.record(s_out)
+    host_submit_s = time.perf_counter() - host_t0
+    for st_ in slot_streams[1:]:
+        ev = torch.cuda.Event()
+        ev.record(st_)
+        slot_streams[0].wait_event(ev)
+    e1.record(slot_streams[0])
     torch.cuda.synchronize()
     barrier()
     pipe.synchronize()
@@ -303,14 +316,17 @@ def run_ours(args):
                                        "launch (profiles/ragged_head_b256_k4096.md); below the "
                                        "algorithmic bytes because repeated rows hit in L2"},
         "e2e": {"value": ROWS * world * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps},
+                "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
+                "host_submit_us_per_step": host_submit_s * 1e6 / args.steps},
         "gpu_launches": args.steps,
-        "timing": {"value": "CUDA graph of the K launches, events around one replay",
+        "timing": {"value": "CUDA graph of the K launches (each may overlap the previous "
+                            "launch's tail: programmatic dependent launch), events around one "
+                            "replay",
                    "roofline": f"per-launch CUDA events over {n_ev} launches",
                    "e2e": "head.HostPipeline.submit_packed: per step one H2D copy of the "
                           "packed batch (hidden + CSR) from pinned host memory, the head, one "
                           f"D2H copy of ids + scores; {PIPE_DEPTH} slots, copies overlap the "
-                          "previous batch's head; events around K steps"},
+                          "other slots' heads; events around K steps"},
         "clocks": clocks.summary(),
     }
     if not args.no_secondary:

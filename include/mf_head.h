@@ -124,6 +124,22 @@ MF_API mf_status mf_head_restricted_csr_f16(const void* hidden, uint64_t hidden_
                                      uint64_t rows, uint64_t hidden_size,
                                      uint64_t vocab, void* stream);
 
+/* mf_head_restricted_csr_f16 with launch options.  MF_LAUNCH_OVERLAP_PREVIOUS:
+ * the launch may begin while the previous kernel on `stream` is still running
+ * (programmatic dependent launch), so back-to-back batches overlap one's
+ * tail with the next one's gathers.  The kernel waits for the previous
+ * kernel before its first write (workspace, outputs), but reads hidden,
+ * offsets, ids and the embedding without waiting: use the flag only when the
+ * previous kernel on the stream does not write them (e.g. consecutive head
+ * calls on independent batches).  Any other bit is invalid_argument. */
+#define MF_LAUNCH_OVERLAP_PREVIOUS 1u
+MF_API mf_status mf_head_restricted_csr_f16_ex(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
+    uint64_t vocab, uint32_t launch_flags, void* stream);
+
 /* The same head with the decoder's final RMSNorm fused in front: `hidden`
  * holds the last layer's un-normalised rows (fp16 [rows, hidden_size]) and
  * gamma the norm weight (fp16 [hidden_size], 16-byte aligned).  Each row is
@@ -259,15 +275,16 @@ MF_API mf_status mf_dense_selftest_wait_timeout(void* stream, uint32_t* error_wo
  *
  * No counterpart in the reference (the reference copies each decode step's
  * inputs and synchronises, src/cuda/smollm2.cu:395-501).  A pipeline owns
- * `depth` device slots and three streams: mf_pipeline_submit copies one batch
- * (hidden fp16 [rows, hidden_size], CSR offsets int32 [rows + 1], ids int32
- * [total_ids]) from host memory to the device, runs the ragged head, and
- * copies ids (u32 [rows]) and scores (f32 [rows], may be NULL) back into the
- * caller's host buffers, asynchronously; the copy-in of the next batch
- * overlaps the head of the current one.  Host buffers should be pinned (a
- * pageable buffer makes its copy synchronous) and must stay untouched until
- * mf_pipeline_wait(ticket) returns.  The embedding stays resident on the
- * device.  mf_pipeline_create allocates the slots (device memory) once. */
+ * `depth` slots, each with a stream, device buffers and its own head
+ * workspace.  mf_pipeline_submit copies one batch (hidden fp16 [rows,
+ * hidden_size], CSR offsets int32 [rows + 1], ids int32 [total_ids]) from
+ * host memory to the next slot, runs the ragged head and copies ids (u32
+ * [rows]) and scores (f32 [rows], may be NULL) back into the caller's host
+ * buffers, all asynchronously on that slot's stream; batches on different
+ * slots overlap.  Host buffers should be pinned (a pageable buffer makes its
+ * copy synchronous) and must stay untouched until mf_pipeline_wait(ticket)
+ * returns.  The embedding stays resident on the device.  mf_pipeline_create
+ * allocates the slots (device memory) once. */
 typedef struct mf_pipeline mf_pipeline;
 
 MF_API mf_status mf_pipeline_create(mf_pipeline** pipeline, const void* embedding,
@@ -287,8 +304,9 @@ MF_API mf_status mf_pipeline_submit_packed(mf_pipeline* pipeline, const void* ba
                                            uint64_t total_ids, void* out, uint64_t* ticket);
 MF_API mf_status mf_pipeline_wait(mf_pipeline* pipeline, uint64_t ticket);
 MF_API mf_status mf_pipeline_synchronize(mf_pipeline* pipeline);
-/* The pipeline's streams: 0 = copy-in, 1 = compute, 2 = copy-out. */
-MF_API void* mf_pipeline_stream(mf_pipeline* pipeline, uint32_t which);
+/* The number of slots, and slot `slot`'s stream (NULL past the last slot). */
+MF_API uint32_t mf_pipeline_depth(mf_pipeline* pipeline);
+MF_API void* mf_pipeline_stream(mf_pipeline* pipeline, uint32_t slot);
 MF_API void mf_pipeline_destroy(mf_pipeline* pipeline);
 
 /* ---- allocation-free ragged head ----------------------------------------

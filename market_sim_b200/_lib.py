@@ -36,6 +36,8 @@ _SIGNATURES = {
                           _P, _U64, _P, _U64, _U64, _U64, _U64, _U64, _U64, _P],
 }
 
+_SIGNATURES["mf_head_restricted_csr_f16_ex"] = ([_P, _U64] * 7 + [_U64, _U64, _U64, ctypes.c_uint32,
+                                                                     _P])
 _SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
                                                      _U64, _P, _U64, _U64, _U64, _U64, _P]
 
@@ -63,7 +65,7 @@ _SIGNATURES["mf_pipeline_synchronize"] = [_P]
 
 _U64_FUNCS = {"mf_head_workspace_bytes": [_U64], "mf_dfa_workspace_bytes": [_U64],
               "mf_dense_workspace_bytes": [_U64], "mf_exchange_bytes": [_U64, ctypes.c_uint32]}
-_U32_FUNCS = {"mf_version": [], "mf_built_arch": []}
+_U32_FUNCS = {"mf_version": [], "mf_built_arch": [], "mf_pipeline_depth": [_P]}
 _PTR_FUNCS = {"mf_pipeline_stream": [_P, ctypes.c_uint32]}
 _VOID_FUNCS = {"mf_pipeline_destroy": [_P]}
 

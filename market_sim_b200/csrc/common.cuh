@@ -59,6 +59,16 @@ __device__ __forceinline__ unsigned long long umax64(unsigned long long a,
   return a > b ? a : b;
 }
 
+// Programmatic dependent launch.  `pdl_trigger` lets the next kernel on the
+// stream (launched with programmatic stream serialization) start while this
+// one is still running; `pdl_wait` blocks until the previous kernel on the
+// stream has completed and its memory is visible.  Both are no-ops for a
+// kernel launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 16-byte streaming load through the read-only path that does not allocate
 // in L1: embedding rows are touched once per candidate.
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {

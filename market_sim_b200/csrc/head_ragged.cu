@@ -225,6 +225,7 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
                           int64_t row_b, int64_t row_e, unsigned long long key, int64_t n,
                           int sub, const BlockSlots& bs) {
   if (sub != 0 || n <= 0) return;
+  pdl_wait();  // the workspace and outputs may still belong to the previous launch
   const int64_t row_len = row_e - row_b;
   if (n == row_len) {  // the group saw the whole row: no merge needed
     finalize_row<M>(p, rows_tab, r, key);
@@ -266,25 +267,15 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   Rows<M> rows_tab;
   int64_t total;
   if (M == RowMode::kCsr) {
+    // Overlapped launches: the next batch's blocks may start as this one's
+    // retire.  Reads of this call's inputs need no wait (the caller promises
+    // the previous kernel does not write them); every write waits (pdl_wait
+    // in flush_row and before the epilogue below).
+    pdl_trigger();
     rows_tab.start = p.offsets;
     total = p.total;
-    // Prologue: empty rows get the sentinel here (no group visits them);
-    // decreasing offsets or a bad first/last offset flag the batch.
-    for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows;
-         r += gridDim.x * kThreads) {
-      const int32_t b = p.offsets[r], e = p.offsets[r + 1];
-      if (e < b) {
-        atomicOr(p.control + 1, 1u);
-      } else if (e == b) {
-        p.out_ids[r] = kInvalid;
-        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
-      }
-    }
-    if (blockIdx.x == 0 && threadIdx.x == 0 &&
-        (p.offsets[0] != 0 || (int64_t)p.offsets[p.rows] != p.total)) {
-      atomicOr(p.control + 1, 1u);
-    }
   } else {
+    pdl_wait();  // a decode step reads the states the previous step wrote
     // Allowed-set lookup: per-sequence candidate counts from the DFA, and
     // their exclusive prefix sum in shared memory (every block computes the
     // same table).  Invalid states and empty sets get the sentinel.
@@ -447,13 +438,30 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     flush_row<M>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
   }
 
+  if constexpr (M == RowMode::kDfa) return;
+  // Empty rows get the sentinel here (no group visits them); decreasing
+  // offsets or a bad first/last offset flag the batch.
+  pdl_wait();
+  for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += gridDim.x * kThreads) {
+    const int32_t b = p.offsets[r], e = p.offsets[r + 1];
+    if (e < b) {
+      atomicOr(p.control + 1, 1u);
+    } else if (e == b) {
+      p.out_ids[r] = kInvalid;
+      if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 &&
+      (p.offsets[0] != 0 || (int64_t)p.offsets[p.rows] != p.total)) {
+    atomicOr(p.control + 1, 1u);
+  }
+
   // Last block out (CSR mode; DFA offsets are built in-kernel and cannot be
   // malformed): if the batch was flagged malformed, give every row the
   // sentinel and clear the whole workspace; then reset the control words.
   // Every thread fences first so its atomics and result stores are ordered
   // before this block's arrival on the done counter (one fence at exit costs
   // less than fencing each store inside the loop).
-  if constexpr (M == RowMode::kDfa) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -578,8 +586,9 @@ static mf_status csr_head(
     const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
     void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
     void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
-    uint64_t vocab, void* stream, const void* gamma, float eps) {
-  if (rows == 0 || hidden_size == 0 || vocab == 0 || stream == nullptr)
+    uint64_t vocab, void* stream, const void* gamma, float eps, uint32_t launch_flags) {
+  if (rows == 0 || hidden_size == 0 || vocab == 0 || stream == nullptr ||
+      (launch_flags & ~MF_LAUNCH_OVERLAP_PREVIOUS) != 0)
     return fail(MF_INVALID_ARGUMENT);
   if (vocab > UINT32_MAX || hidden_size > UINT32_MAX || rows > (uint64_t)INT32_MAX - 1)
     return fail(MF_RESOURCE_LIMIT);
@@ -621,16 +630,28 @@ static mf_status csr_head(
   const int64_t groups = blocks * kGroupsPerBlock;
   int64_t chunk = (p.total + groups - 1) / groups;
   if (chunk < 1) chunk = 1;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  if (launch_flags & MF_LAUNCH_OVERLAP_PREVIOUS) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e;
   if (fast && p.gamma)
-    ragged_head_kernel<RowMode::kCsr, true, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+    e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, true, true>, p, chunk);
   else if (fast)
-    ragged_head_kernel<RowMode::kCsr, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+    e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, true>, p, chunk);
   else if (p.gamma)
-    ragged_head_kernel<RowMode::kCsr, false, true><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
+    e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, false, true>, p, chunk);
   else
-    ragged_head_kernel<RowMode::kCsr, false><<<(unsigned)blocks, kThreads, 0, s>>>(p, chunk);
-  return launch_status(cudaGetLastError());
+    e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, false>, p, chunk);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return launch_status(e);
 }
 
 extern "C" mf_status mf_head_restricted_csr_f16(
@@ -641,7 +662,18 @@ extern "C" mf_status mf_head_restricted_csr_f16(
     uint64_t vocab, void* stream) {
   return csr_head(hidden, hidden_bytes, embedding, embedding_bytes, offsets, offsets_bytes, ids,
                   ids_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes, workspace,
-                  workspace_bytes, rows, hidden_size, vocab, stream, nullptr, 0.f);
+                  workspace_bytes, rows, hidden_size, vocab, stream, nullptr, 0.f, 0u);
+}
+
+extern "C" mf_status mf_head_restricted_csr_f16_ex(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
+    uint64_t vocab, uint32_t launch_flags, void* stream) {
+  return csr_head(hidden, hidden_bytes, embedding, embedding_bytes, offsets, offsets_bytes, ids,
+                  ids_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes, workspace,
+                  workspace_bytes, rows, hidden_size, vocab, stream, nullptr, 0.f, launch_flags);
 }
 
 extern "C" mf_status mf_head_restricted_csr_rmsnorm_f16(
@@ -659,7 +691,7 @@ extern "C" mf_status mf_head_restricted_csr_rmsnorm_f16(
     return fail(MF_INVALID_ARGUMENT);
   return csr_head(hidden, hidden_bytes, embedding, embedding_bytes, offsets, offsets_bytes, ids,
                   ids_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes, workspace,
-                  workspace_bytes, rows, hidden_size, vocab, stream, gamma, eps);
+                  workspace_bytes, rows, hidden_size, vocab, stream, gamma, eps, 0u);
 }
 
 namespace {

@@ -1,10 +1,13 @@
 // Native host pipeline for the ragged head: batches that live in host memory
-// go H2D on a copy stream, through the head on a compute stream, and their
-// ids and scores come back D2H on a third stream, with `depth` device slots
-// rotating so the copy-in of batch i + 1 overlaps the head of batch i.  All
-// per-batch work is native (a handful of async CUDA calls), so the host
-// keeps ahead of a ~25 us head.  Host buffers should be pinned: a pageable
-// buffer makes its copy synchronous (still correct, no overlap).
+// go H2D, through the head and back D2H, with `depth` slots in flight.  Each
+// slot owns a stream, its device buffers and its own head workspace, so one
+// batch is three stream-ordered operations (copy in, head, copy out) plus
+// the event mf_pipeline_wait uses; a slot's next batch queues behind its
+// previous one on the same stream, and batches on different slots overlap
+// (copies of one with the head of another, and one head's tail with the
+// next head).  All per-batch work is native, so the host keeps ahead of a
+// ~20 us head.  Host buffers should be pinned: a pageable buffer makes its
+// copy synchronous (still correct, no overlap).
 #include <cuda_runtime.h>
 
 #include <new>
@@ -21,8 +24,9 @@ namespace {
 struct Slot {
   void* in = nullptr;
   void* out = nullptr;
-  cudaEvent_t loaded = nullptr, ran = nullptr, done = nullptr;
-  bool used = false;
+  void* workspace = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t done = nullptr;
 };
 
 }  // namespace
@@ -31,8 +35,6 @@ struct mf_pipeline {
   int device = 0;
   const void* embedding = nullptr;
   uint64_t embedding_bytes = 0, vocab = 0, hidden_size = 0, max_rows = 0, max_ids = 0;
-  cudaStream_t s_in = nullptr, s_run = nullptr, s_out = nullptr;
-  void* workspace = nullptr;
   std::vector<Slot> slots;
   uint64_t submitted = 0;
 
@@ -52,18 +54,42 @@ void release(mf_pipeline* p) {
   cudaGetDevice(&prev);
   cudaSetDevice(p->device);
   for (auto& s : p->slots) {
+    if (s.stream) cudaStreamSynchronize(s.stream);
     cudaFree(s.in);
     cudaFree(s.out);
-    if (s.loaded) cudaEventDestroy(s.loaded);
-    if (s.ran) cudaEventDestroy(s.ran);
+    cudaFree(s.workspace);
     if (s.done) cudaEventDestroy(s.done);
+    if (s.stream) cudaStreamDestroy(s.stream);
   }
-  cudaFree(p->workspace);
-  if (p->s_in) cudaStreamDestroy(p->s_in);
-  if (p->s_run) cudaStreamDestroy(p->s_run);
-  if (p->s_out) cudaStreamDestroy(p->s_out);
   cudaSetDevice(prev);
   delete p;
+}
+
+// The head and the copy-out of one batch already copied into slot `s`: one
+// copy of ids + scores when `joined` (the caller's packed output buffer),
+// else one per buffer.  Adjacent addresses alone do not make a buffer
+// packed: two pinned allocations can be neighbours, and one copy across both
+// is invalid.
+mf_status run_and_return(mf_pipeline* p, Slot& s, uint64_t rows, uint64_t total_ids,
+                         void* out_ids, void* out_scores, bool joined, uint64_t* ticket) {
+  const uint64_t hb = rows * p->hidden_size * 2;
+  char* in = static_cast<char*>(s.in);
+  char* out = static_cast<char*>(s.out);
+  const mf_status h = mf_head_restricted_csr_f16(
+      in, hb, p->embedding, p->embedding_bytes, in + hb, (rows + 1) * 4,
+      total_ids ? in + hb + (rows + 1) * 4 : nullptr, total_ids * 4, out, rows * 4,
+      out + rows * 4, rows * 4, s.workspace, mf_head_workspace_bytes(rows), rows,
+      p->hidden_size, p->vocab, s.stream);
+  if (h.code != MF_OK) return h;
+  cudaError_t e =
+      cudaMemcpyAsync(out_ids, out, rows * (joined ? 8 : 4), cudaMemcpyDeviceToHost, s.stream);
+  if (e == cudaSuccess && out_scores && !joined)
+    e = cudaMemcpyAsync(out_scores, out + rows * 4, rows * 4, cudaMemcpyDeviceToHost, s.stream);
+  if (e == cudaSuccess) e = cudaEventRecord(s.done, s.stream);
+  if (e != cudaSuccess) return st_rt(e);
+  if (ticket) *ticket = p->submitted;
+  ++p->submitted;
+  return st_ok();
 }
 
 }  // namespace
@@ -87,18 +113,17 @@ extern "C" mf_status mf_pipeline_create(mf_pipeline** out, const void* embedding
   p->max_rows = max_rows;
   p->max_ids = max_ids;
   cudaError_t e = cudaGetDevice(&p->device);
-  for (cudaStream_t* s : {&p->s_in, &p->s_run, &p->s_out})
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
   const uint64_t ws = mf_head_workspace_bytes(max_rows);
-  if (e == cudaSuccess) e = cudaMalloc(&p->workspace, ws);
-  if (e == cudaSuccess) e = cudaMemset(p->workspace, 0, ws);
   p->slots.resize(depth);
   for (auto& s : p->slots) {
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&s.in, p->packed_bytes(max_rows, max_ids));
     if (e == cudaSuccess) e = cudaMalloc(&s.out, max_rows * 8);
-    for (cudaEvent_t* ev : {&s.loaded, &s.ran, &s.done})
-      if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMalloc(&s.workspace, ws);
+    if (e == cudaSuccess) e = cudaMemset(s.workspace, 0, ws);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming);
   }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // the workspaces are zero before use
   if (e != cudaSuccess) {
     release(p);
     return st_rt(e);
@@ -106,43 +131,6 @@ extern "C" mf_status mf_pipeline_create(mf_pipeline** out, const void* embedding
   *out = p;
   return st_ok();
 }
-
-namespace {
-
-// Everything after the copy-in of one batch into slot `s`: the head on the
-// compute stream, then the copy-out: one copy of ids + scores when `joined`
-// (the caller's packed output buffer), else one per buffer.  Adjacent
-// addresses alone do not make a buffer packed: two pinned allocations can be
-// neighbours, and one copy across both is invalid.
-mf_status run_and_return(mf_pipeline* p, Slot& s, uint64_t rows, uint64_t total_ids,
-                         void* out_ids, void* out_scores, bool joined, uint64_t* ticket) {
-  cudaError_t e = cudaEventRecord(s.loaded, p->s_in);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_run, s.loaded, 0);
-  if (e != cudaSuccess) return st_rt(e);
-  const uint64_t hb = rows * p->hidden_size * 2;
-  char* in = static_cast<char*>(s.in);
-  char* out = static_cast<char*>(s.out);
-  const mf_status h = mf_head_restricted_csr_f16(
-      in, hb, p->embedding, p->embedding_bytes, in + hb, (rows + 1) * 4,
-      total_ids ? in + hb + (rows + 1) * 4 : nullptr, total_ids * 4, out, rows * 4,
-      out + rows * 4, rows * 4, p->workspace, mf_head_workspace_bytes(rows), rows,
-      p->hidden_size, p->vocab, p->s_run);
-  if (h.code != MF_OK) return h;
-  e = cudaEventRecord(s.ran, p->s_run);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_out, s.ran, 0);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(out_ids, out, rows * (joined ? 8 : 4), cudaMemcpyDeviceToHost, p->s_out);
-  if (e == cudaSuccess && out_scores && !joined)
-    e = cudaMemcpyAsync(out_scores, out + rows * 4, rows * 4, cudaMemcpyDeviceToHost, p->s_out);
-  if (e == cudaSuccess) e = cudaEventRecord(s.done, p->s_out);
-  if (e != cudaSuccess) return st_rt(e);
-  s.used = true;
-  if (ticket) *ticket = p->submitted;
-  ++p->submitted;
-  return st_ok();
-}
-
-}  // namespace
 
 extern "C" mf_status mf_pipeline_submit(mf_pipeline* p, const void* hidden, uint64_t rows,
                                         const void* offsets, const void* ids, uint64_t total_ids,
@@ -152,16 +140,14 @@ extern "C" mf_status mf_pipeline_submit(mf_pipeline* p, const void* hidden, uint
     return mf_status{MF_INVALID_ARGUMENT, 0};
   if (rows > p->max_rows || total_ids > p->max_ids) return mf_status{MF_RESOURCE_LIMIT, 0};
   Slot& s = p->slots[p->submitted % p->slots.size()];
-  cudaError_t e = cudaSuccess;
-  if (s.used) e = cudaStreamWaitEvent(p->s_in, s.done, 0);  // slot's previous batch is home
   const uint64_t hb = rows * p->hidden_size * 2;
   char* in = static_cast<char*>(s.in);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(in, hidden, hb, cudaMemcpyHostToDevice, p->s_in);
+  cudaError_t e = cudaMemcpyAsync(in, hidden, hb, cudaMemcpyHostToDevice, s.stream);
   if (e == cudaSuccess)
-    e = cudaMemcpyAsync(in + hb, offsets, (rows + 1) * 4, cudaMemcpyHostToDevice, p->s_in);
+    e = cudaMemcpyAsync(in + hb, offsets, (rows + 1) * 4, cudaMemcpyHostToDevice, s.stream);
   if (e == cudaSuccess && total_ids)
     e = cudaMemcpyAsync(in + hb + (rows + 1) * 4, ids, total_ids * 4, cudaMemcpyHostToDevice,
-                        p->s_in);
+                        s.stream);
   if (e != cudaSuccess) return st_rt(e);
   return run_and_return(p, s, rows, total_ids, out_ids, out_scores, false, ticket);
 }
@@ -175,9 +161,8 @@ extern "C" mf_status mf_pipeline_submit_packed(mf_pipeline* p, const void* batch
   if (rows > p->max_rows || total_ids > p->max_ids) return mf_status{MF_RESOURCE_LIMIT, 0};
   if (batch_bytes != p->packed_bytes(rows, total_ids)) return mf_status{MF_INVALID_ARGUMENT, 0};
   Slot& s = p->slots[p->submitted % p->slots.size()];
-  cudaError_t e = cudaSuccess;
-  if (s.used) e = cudaStreamWaitEvent(p->s_in, s.done, 0);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(s.in, batch, batch_bytes, cudaMemcpyHostToDevice, p->s_in);
+  const cudaError_t e =
+      cudaMemcpyAsync(s.in, batch, batch_bytes, cudaMemcpyHostToDevice, s.stream);
   if (e != cudaSuccess) return st_rt(e);
   return run_and_return(p, s, rows, total_ids, out, static_cast<char*>(out) + rows * 4, true,
                         ticket);
@@ -192,16 +177,20 @@ extern "C" mf_status mf_pipeline_wait(mf_pipeline* p, uint64_t ticket) {
 
 extern "C" mf_status mf_pipeline_synchronize(mf_pipeline* p) {
   if (p == nullptr) return mf_status{MF_INVALID_ARGUMENT, 0};
-  const cudaError_t e = cudaStreamSynchronize(p->s_out);
-  return e == cudaSuccess ? st_ok() : st_rt(e);
+  for (auto& s : p->slots) {
+    const cudaError_t e = cudaStreamSynchronize(s.stream);
+    if (e != cudaSuccess) return st_rt(e);
+  }
+  return st_ok();
 }
 
-extern "C" void* mf_pipeline_stream(mf_pipeline* p, uint32_t which) {
-  if (!p) return nullptr;
-  return which == 0 ? (void*)p->s_in : which == 1 ? (void*)p->s_run : (void*)p->s_out;
+extern "C" uint32_t mf_pipeline_depth(mf_pipeline* p) {
+  return p ? (uint32_t)p->slots.size() : 0u;
 }
 
-extern "C" void mf_pipeline_destroy(mf_pipeline* p) {
-  if (p) cudaStreamSynchronize(p->s_out);
-  release(p);
+extern "C" void* mf_pipeline_stream(mf_pipeline* p, uint32_t slot) {
+  if (!p || slot >= p->slots.size()) return nullptr;
+  return (void*)p->slots[slot].stream;
 }
+
+extern "C" void mf_pipeline_destroy(mf_pipeline* p) { release(p); }

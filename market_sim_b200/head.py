@@ -252,6 +252,23 @@ def restricted_output_head_csr_f16(hidden: Buffer, embedding: Buffer, offsets: B
         *_pb(workspace), rows, hidden_size, vocabulary_size, _sp(stream)))
 
 
+LAUNCH_OVERLAP_PREVIOUS = 1
+"""``restricted_output_head_csr_f16_ex`` flag: the launch may overlap the tail
+of the previous kernel on the stream, which must not write this call's
+inputs (consecutive head calls on independent batches)."""
+
+
+def restricted_output_head_csr_f16_ex(hidden: Buffer, embedding: Buffer, offsets: Buffer,
+                                      ids: Buffer, token_ids: Buffer, scores: Optional[Buffer],
+                                      workspace: Buffer, rows: int, hidden_size: int,
+                                      vocabulary_size: int, launch_flags: int, stream) -> Status:
+    """``restricted_output_head_csr_f16`` with launch options
+    (``LAUNCH_OVERLAP_PREVIOUS``)."""
+    return _status(lib.mf_head_restricted_csr_f16_ex(
+        *_pb(hidden), *_pb(embedding), *_pb(offsets), *_pb(ids), *_pb(token_ids), *_pb(scores),
+        *_pb(workspace), rows, hidden_size, vocabulary_size, launch_flags, _sp(stream)))
+
+
 NOALLOC_MAX_ROWS = 65536
 """Largest batch ``restricted_output_head_csr_f16_noalloc`` accepts."""
 
@@ -462,11 +479,11 @@ class RaggedHead:
 class HostPipeline:
     """Restricted head over batches that live in host memory (native
     ``mf_pipeline_*``): each ``submit`` copies one batch (hidden rows, CSR
-    offsets, CSR ids) from pinned host memory to the device on a copy stream,
-    runs the ragged head on a compute stream and copies ids and scores back
-    into pinned host memory on a third stream; ``depth`` device slots rotate,
-    so the copy-in of batch i + 1 overlaps the head of batch i.  Host tensors
-    must stay untouched until ``wait(ticket)`` returns.
+    offsets, CSR ids) from pinned host memory to the device, runs the ragged
+    head and copies ids and scores back into pinned host memory, in order on
+    the stream of the next of ``depth`` slots (each slot has its own device
+    buffers and workspace), so batches on different slots overlap.  Host
+    tensors must stay untouched until ``wait(ticket)`` returns.
     """
 
     def __init__(self, embedding, max_rows: int, max_ids: int, depth: int = 6, device=None):
@@ -481,9 +498,13 @@ class HostPipeline:
         if not st.ok():
             raise RuntimeError(f"mf_pipeline_create failed: {st}")
 
-    def stream(self, which: int) -> int:
-        """cudaStream_t of the copy-in (0), compute (1) or copy-out (2) stream."""
-        return int(lib.mf_pipeline_stream(self._p, which) or 0)
+    def depth(self) -> int:
+        """Number of slots (batches in flight)."""
+        return int(lib.mf_pipeline_depth(self._p))
+
+    def stream(self, slot: int) -> int:
+        """cudaStream_t of slot ``slot`` (copy in, head, copy out in order)."""
+        return int(lib.mf_pipeline_stream(self._p, slot) or 0)
 
     def submit(self, hidden, offsets, ids, out_ids, out_scores=None) -> int:
         """hidden fp16 [rows, H], offsets int32 [rows + 1], ids int32 [total],

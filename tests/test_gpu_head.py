@@ -466,3 +466,57 @@ def test_fused_rmsnorm_rejects(mf):
     assert f(x, g, float("nan"), e, off, ids, out, None, ws, rows, hs, v, s).code == E.invalid_argument
     assert f(x, g[:100], 1e-5, e, off, ids, out, None, ws, rows, hs, v, s).code == E.invalid_argument
     assert f(x, g, 1e-5, e, off, ids, out, None, ws, rows, hs, v, s).ok()
+
+
+def test_overlapped_launches_match_plain_calls(mf, emb_full):
+    """MF_LAUNCH_OVERLAP_PREVIOUS: back-to-back launches on independent
+    batches sharing one workspace (eagerly and inside a CUDA graph), each
+    writing its own outputs or all writing the same ones, equal plain calls;
+    the workspace is left zero; unknown flag bits are rejected."""
+    import torch
+
+    e, e_dev = emb_full
+    cases = [_ragged_case(800 + i, rows, kmax) for i, (rows, kmax) in
+             enumerate([(256, 4096), (256, 4096), (64, 512), (256, 4096), (3, 40), (256, 2048)])]
+    want = [_csr_call(mf, h, e_dev, off, ids)[:2] for h, off, ids in cases]
+    dev = [(to_dev(h), to_dev(off), to_dev(ids)) for h, off, ids in cases]
+    ws = torch.zeros(mf.head_workspace_bytes(256), dtype=torch.uint8, device="cuda")
+    s = gpu_stream()
+    flag = mf.LAUNCH_OVERLAP_PREVIOUS
+
+    def launch(j, out, sc):
+        h, off, ids = dev[j]
+        st = mf.restricted_output_head_csr_f16_ex(h, e_dev, off, ids, out, sc, ws, len(cases[j][0]),
+                                                  576, 49_152, flag, s)
+        assert st.ok(), st
+
+    outs = [(torch.empty(len(c[0]), dtype=torch.int32, device="cuda"),
+             torch.empty(len(c[0]), dtype=torch.float32, device="cuda")) for c in cases]
+    with torch.cuda.stream(s):
+        for rep in range(4):
+            for j in range(len(cases)):
+                launch(j, *outs[j])
+    s.synchronize()
+    for (o, sc), (wi, ws_) in zip(outs, want):
+        assert np.array_equal(_u32(o), wi)
+        assert np.array_equal(sc.cpu().numpy().view(np.uint32), ws_.view(np.uint32))
+    assert int(ws.sum()) == 0
+
+    shared = (torch.empty(256, dtype=torch.int32, device="cuda"),
+              torch.empty(256, dtype=torch.float32, device="cuda"))
+    g = torch.cuda.CUDAGraph()
+    order = [0, 1, 3, 5, 0, 1, 3, 5, 1, 3]  # all 256-row batches; the last one wins
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for j in order:
+                launch(j, *shared)
+        for _ in range(3):
+            g.replay()
+    s.synchronize()
+    assert np.array_equal(_u32(shared[0]), want[order[-1]][0])
+    assert int(ws.sum()) == 0
+
+    h, off, ids = dev[0]
+    st = mf.restricted_output_head_csr_f16_ex(h, e_dev, off, ids, *shared, ws, 256, 576, 49_152,
+                                              2, s)
+    assert st.code == mf.ErrorCode.invalid_argument
