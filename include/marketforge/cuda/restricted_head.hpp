@@ -27,6 +27,16 @@ namespace marketforge::cuda {
     DeviceBuffer& workspace, std::uint64_t rows, std::uint64_t hidden_size,
     std::uint64_t vocabulary_size, StreamHandle stream) noexcept;
 
+// Launch option of the overload below (MF_LAUNCH_OVERLAP_PREVIOUS): the call
+// may overlap the tail of the previous kernel on `stream`, which must not
+// write this call's inputs (consecutive calls on independent batches).
+inline constexpr std::uint32_t launch_overlap_previous = 1u;
+[[nodiscard]] Status restricted_output_head_csr_f16(
+    const DeviceBuffer& hidden, const DeviceBuffer& embedding, const DeviceBuffer& offsets,
+    const DeviceBuffer& ids, DeviceBuffer& token_ids, DeviceBuffer& scores,
+    DeviceBuffer& workspace, std::uint64_t rows, std::uint64_t hidden_size,
+    std::uint64_t vocabulary_size, std::uint32_t launch_flags, StreamHandle stream) noexcept;
+
 // The same with the final RMSNorm fused in front: hidden holds the last
 // layer's un-normalised rows, gamma the norm weight fp16 [hidden_size]
 // (replaces rms_norm_f16 + the head, src/cuda/smollm2.cu:474-492).
@@ -53,6 +63,17 @@ namespace marketforge::cuda {
     const DeviceBuffer& hidden, const DeviceBuffer& embedding, DeviceBuffer& keys,
     DeviceBuffer& token_ids, DeviceBuffer& workspace, std::uint64_t rows,
     std::uint64_t hidden_size, std::uint64_t vocab_rows, std::uint64_t vocab_begin,
+    StreamHandle stream) noexcept;
+
+// Vocabulary shards on several GPUs, merged inside the kernel
+// (mf_dense_head_sharded_f16): one process per GPU; exchange[q] is rank q's
+// exchange buffer (mf_exchange_alloc / mf_exchange_open_peer) as mapped in
+// this process; every rank gets the global ids (and merged keys).
+[[nodiscard]] Status dense_output_head_sharded_f16(
+    const DeviceBuffer& hidden, const DeviceBuffer& embedding, DeviceBuffer& keys,
+    DeviceBuffer& token_ids, DeviceBuffer& workspace, std::uint64_t rows,
+    std::uint64_t hidden_size, std::uint64_t vocab_rows, std::uint64_t vocab_begin,
+    void* const* exchange, std::uint64_t exchange_bytes, std::uint32_t world, std::uint32_t rank,
     StreamHandle stream) noexcept;
 
 }  // namespace marketforge::cuda

@@ -275,7 +275,8 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     rows_tab.start = p.offsets;
     total = p.total;
   } else {
-    pdl_wait();  // a decode step reads the states the previous step wrote
+    pdl_trigger();  // the next decode step's blocks may queue behind this one's
+    pdl_wait();     // a decode step reads the states the previous step wrote
     // Allowed-set lookup: per-sequence candidate counts from the DFA, and
     // their exclusive prefix sum in shared memory (every block computes the
     // same table).  Invalid states and empty sets get the sentinel.
@@ -721,15 +722,29 @@ mf_status dfa_validate(const void* hidden, uint64_t hidden_bytes, const void* em
   return ok();
 }
 
-cudaError_t dfa_launch(RaggedParams p, bool fast, cudaStream_t s) {
+// `after_step`: the previous kernel on `s` is the previous decode step, so
+// this step launches as its programmatic dependent (its blocks take SM
+// slots as the previous step's retire and wait in griddepcontrol.wait).
+cudaError_t dfa_launch(RaggedParams p, bool fast, cudaStream_t s, bool after_step) {
   DeviceInfo& d = device_info();
   const int64_t blocks = (int64_t)d.sms * d.blocks_per_sm[1][fast ? 1 : 0];
-  const size_t smem = (2 * (size_t)p.rows + 1) * sizeof(int32_t);  // <= 64 KB
-  if (fast)
-    ragged_head_kernel<RowMode::kDfa, true><<<(unsigned)blocks, kThreads, smem, s>>>(p, 0);
-  else
-    ragged_head_kernel<RowMode::kDfa, false><<<(unsigned)blocks, kThreads, smem, s>>>(p, 0);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (2 * (size_t)p.rows + 1) * sizeof(int32_t);  // <= 64 KB
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (after_step) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = fast ? cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, true>, p,
+                                            (int64_t)0)
+                       : cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, false>, p,
+                                            (int64_t)0);
+  return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 }  // namespace
@@ -769,7 +784,7 @@ extern "C" mf_status mf_dfa_head_step_f16(
   p.vocab = (uint32_t)vocab;
   split_workspace(workspace, batch, p);
   return launch_status(dfa_launch(p, fast_path(hidden, embedding, hidden_size),
-                                  static_cast<cudaStream_t>(stream)));
+                                  static_cast<cudaStream_t>(stream), false));
 }
 
 extern "C" mf_status mf_dfa_decode_f16(
@@ -809,7 +824,7 @@ extern "C" mf_status mf_dfa_decode_f16(
     p.hidden_size = (uint32_t)hidden_size;
     p.vocab = (uint32_t)vocab;
     split_workspace(workspace, batch, p);
-    const cudaError_t e = dfa_launch(p, fast, s);
+    const cudaError_t e = dfa_launch(p, fast, s, step > 0);
     if (e != cudaSuccess) return launch_status(e);
   }
   return ok();

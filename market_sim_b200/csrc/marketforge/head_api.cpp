@@ -110,4 +110,33 @@ Status dense_output_head_f16(const DeviceBuffer& hidden, const DeviceBuffer& emb
       st(stream)));
 }
 
+Status restricted_output_head_csr_f16(const DeviceBuffer& hidden, const DeviceBuffer& embedding,
+                                      const DeviceBuffer& offsets, const DeviceBuffer& ids,
+                                      DeviceBuffer& token_ids, DeviceBuffer& scores,
+                                      DeviceBuffer& workspace, std::uint64_t rows,
+                                      std::uint64_t hidden_size, std::uint64_t vocabulary_size,
+                                      std::uint32_t launch_flags, StreamHandle stream) noexcept {
+  return to_status(mf_head_restricted_csr_f16_ex(
+      ca(hidden), hidden.size_bytes(), ca(embedding), embedding.size_bytes(), ca(offsets),
+      offsets.size_bytes(), ids.address().valid() ? ca(ids) : nullptr, ids.size_bytes(),
+      ma(token_ids), token_ids.size_bytes(), scores.address().valid() ? ma(scores) : nullptr,
+      scores.size_bytes(), ma(workspace), workspace.size_bytes(), rows, hidden_size,
+      vocabulary_size, launch_flags, st(stream)));
+}
+
+Status dense_output_head_sharded_f16(const DeviceBuffer& hidden, const DeviceBuffer& embedding,
+                                     DeviceBuffer& keys, DeviceBuffer& token_ids,
+                                     DeviceBuffer& workspace, std::uint64_t rows,
+                                     std::uint64_t hidden_size, std::uint64_t vocab_rows,
+                                     std::uint64_t vocab_begin, void* const* exchange,
+                                     std::uint64_t exchange_bytes, std::uint32_t world,
+                                     std::uint32_t rank, StreamHandle stream) noexcept {
+  return to_status(mf_dense_head_sharded_f16(
+      ca(hidden), hidden.size_bytes(), ca(embedding), embedding.size_bytes(),
+      keys.address().valid() ? ma(keys) : nullptr, keys.size_bytes(),
+      token_ids.address().valid() ? ma(token_ids) : nullptr, token_ids.size_bytes(), nullptr, 0,
+      ma(workspace), workspace.size_bytes(), rows, hidden_size, vocab_rows, vocab_begin, exchange,
+      exchange_bytes, world, rank, st(stream)));
+}
+
 }  // namespace marketforge::cuda

@@ -14,6 +14,7 @@
 
 #include "marketforge/cuda/greedy.hpp"
 #include "marketforge/cuda/restricted_head.hpp"
+#include "mf_head.h"
 
 using marketforge::ErrorCode;
 using namespace marketforge::cuda;
@@ -142,6 +143,22 @@ static void new_entry_points(const CudaStream& s) {
   for (uint64_t r = 0; r < rows; ++r) same += ragged[r] == dense[r];
   CHECK(same >= (int)rows - 2);  // FP32 summation order may flip a near-tie
   for (float v : scores) CHECK(std::isfinite(v));
+
+  // overlapped back-to-back launches give the same ids as the plain call
+  auto out2 = std::move(DeviceBuffer::allocate(rows * 4)).value();
+  CHECK(restricted_output_head_csr_f16(h, e, o, i, out, sc, ws, rows, hs, vocab,
+                                       launch_overlap_previous, s.handle()).ok());
+  CHECK(restricted_output_head_csr_f16(h, e, o, i, out2, sc, ws, rows, hs, vocab,
+                                       launch_overlap_previous, s.handle()).ok());
+  CHECK(download<uint32_t>(out, rows, s) == ragged);
+  CHECK(download<uint32_t>(out2, rows, s) == ragged);
+
+  // the sharded dense head with one rank (its own exchange buffer) equals the dense head
+  auto xb = std::move(DeviceBuffer::allocate(mf_exchange_bytes(rows, 1))).value();
+  void* exchange[1] = {reinterpret_cast<void*>(xb.address().value)};
+  CHECK(dense_output_head_sharded_f16(h, e, no_keys, out, ws, rows, hs, vocab, 0, exchange,
+                                      xb.size_bytes(), 1, 0, s.handle()).ok());
+  CHECK(download<uint32_t>(out, rows, s) == dense);
 }
 
 int main() {
