@@ -376,12 +376,15 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
     ex = head.VocabShardExchange(DENSE_ROWS) if world > 1 else None
 
     def step(i):
+        # consecutive steps are independent: each launch may start while the
+        # previous one drains (programmatic dependent launch)
         if world > 1:
             st = head.dense_head_sharded_f16(hid, shards[i % len(shards)], None, ids, None, ws,
-                                             DENSE_ROWS, 576, per, v0, ex, h)
+                                             DENSE_ROWS, 576, per, v0, ex, h,
+                                             head.LAUNCH_OVERLAP_PREVIOUS)
         else:
-            st = head.dense_head_f16(hid, shards[i % len(shards)], None, ids, None, ws,
-                                     DENSE_ROWS, 576, per, v0, h)
+            st = head.dense_head_f16_ex(hid, shards[i % len(shards)], None, ids, None, ws,
+                                        DENSE_ROWS, 576, per, v0, head.LAUNCH_OVERLAP_PREVIOUS, h)
         if not st.ok():
             raise RuntimeError(f"dense head failed: {st}")
 

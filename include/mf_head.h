@@ -228,6 +228,20 @@ MF_API mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes,
                                    uint64_t rows, uint64_t hidden_size,
                                    uint64_t vocab_rows, uint64_t vocab_begin, void* stream);
 
+/* mf_dense_head_f16 with launch options (MF_LAUNCH_OVERLAP_PREVIOUS, declared
+ * with mf_head_restricted_csr_f16_ex): the launch may start while the
+ * previous kernel on `stream` drains; it reads hidden and embedding without
+ * waiting and waits before its first write, so the previous kernel must not
+ * write hidden or embedding. */
+MF_API mf_status mf_dense_head_f16_ex(const void* hidden, uint64_t hidden_bytes,
+                                      const void* embedding, uint64_t embedding_bytes,
+                                      void* out_keys, uint64_t out_keys_bytes, void* out_ids,
+                                      uint64_t out_ids_bytes, void* out_scores,
+                                      uint64_t out_scores_bytes, void* workspace,
+                                      uint64_t workspace_bytes, uint64_t rows,
+                                      uint64_t hidden_size, uint64_t vocab_rows,
+                                      uint64_t vocab_begin, uint32_t launch_flags, void* stream);
+
 /* Decodes packed keys (e.g. after a max all-reduce across vocabulary shards)
  * to ids u32 [rows] and, if out_scores is not NULL, FP32 scores. */
 MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out_ids,
@@ -249,7 +263,8 @@ MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out
  * exchange[q] is rank q's buffer as mapped in this process (the own buffer
  * at exchange[rank]); world <= 8; every rank calls with the same rows, in
  * the same order, on its own GPU.  A rank whose peers do not arrive within
- * 100 ms gives every row the sentinel; the context stays usable. */
+ * 100 ms gives every row the sentinel; the context stays usable.
+ * launch_flags as for mf_dense_head_f16_ex. */
 #define MF_IPC_HANDLE_BYTES 64
 MF_API uint64_t mf_exchange_bytes(uint64_t rows, uint32_t world);
 MF_API mf_status mf_exchange_alloc(void** buffer, uint64_t bytes, void* ipc_handle);
@@ -262,7 +277,7 @@ MF_API mf_status mf_dense_head_sharded_f16(
     void* out_scores, uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes,
     uint64_t rows, uint64_t hidden_size, uint64_t vocab_rows, uint64_t vocab_begin,
     void* const* exchange, uint64_t exchange_bytes, uint32_t world, uint32_t rank,
-    void* stream);
+    uint32_t launch_flags, void* stream);
 
 /* Self-test of the dense kernel's bounded waits (no counterpart in the
  * reference): a tiny dense problem whose loads are never issued, so its

@@ -264,6 +264,11 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
   const uint32_t q = pair / p.m_tiles;  // position in the vocabulary walk
   const uint32_t my_tiles = q < p.n_tiles ? (p.n_tiles - q + p.per_m - 1) / p.per_m : 0;
   const bool leader = rank == 0;
+  // Overlapped launches (MF_LAUNCH_OVERLAP_PREVIOUS): the next launch's CTA
+  // pairs may take SMs as this launch's retire and run their tiles; every
+  // write to the workspace or the outputs waits for the previous launch
+  // (pdl_wait before the key merge and at teardown).
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     bar_init(a_full, 1);
@@ -408,11 +413,13 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       const unsigned long long key =
           best_col != 0xFFFFFFFFu ? make_key(best, p.vocab_begin + best_col)
                                   : make_key(qnan, p.vocab_begin);
+      pdl_wait();
       atomicMax(p.keys + row, key);
     }
   }
 
   // ---- teardown: drain the producers' copies, free TMEM ----
+  pdl_wait();
   __syncthreads();
   if (*abort_flag && threadIdx.x == 0) {
     atomicOr(p.control + 1, 1u);
@@ -622,8 +629,9 @@ mf_status dense_launch(const void* hidden, uint64_t hidden_bytes, const void* em
                        uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes,
                        uint64_t rows, uint64_t hidden_size, uint64_t vocab_rows,
                        uint64_t vocab_begin, uint32_t world, uint32_t rank,
-                       unsigned char* const* xbuf, void* stream) {
-  if (rows == 0 || hidden_size == 0 || vocab_rows == 0 || stream == nullptr)
+                       unsigned char* const* xbuf, uint32_t launch_flags, void* stream) {
+  if (rows == 0 || hidden_size == 0 || vocab_rows == 0 || stream == nullptr ||
+      (launch_flags & ~MF_LAUNCH_OVERLAP_PREVIOUS) != 0)
     return d_fail(MF_INVALID_ARGUMENT);
   if (hidden_size % kBK != 0 || hidden_size > (uint64_t)kMaxKChunks * kBK)
     return d_fail(MF_RESOURCE_LIMIT);  // widths 64..576 in steps of 64
@@ -671,10 +679,20 @@ mf_status dense_launch(const void* hidden, uint64_t hidden_bytes, const void* em
       !make_map(&tm_e, embedding, vocab_rows, hidden_size, kBNHalf))
     return d_fail(MF_CUDA_RUNTIME_FAILURE);
 
-  const unsigned grid = 2 * p.m_tiles * p.per_m;  // CTA pairs (cluster dims 2)
-  dense_head_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tm_h, tm_e,
-                                                                                      p);
-  e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * p.m_tiles * p.per_m, 1, 1);  // CTA pairs (cluster dims 2)
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  if (launch_flags & MF_LAUNCH_OVERLAP_PREVIOUS) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, dense_head_kernel, tm_h, tm_e, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_BACKEND_FAILURE, (uint32_t)e);
 }
 
@@ -691,7 +709,22 @@ extern "C" mf_status mf_dense_head_f16(const void* hidden, uint64_t hidden_bytes
   return dense_launch(hidden, hidden_bytes, embedding, embedding_bytes, out_keys,
                       out_keys_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes,
                       workspace, workspace_bytes, rows, hidden_size, vocab_rows, vocab_begin, 1u,
-                      0u, nullptr, stream);
+                      0u, nullptr, 0u, stream);
+}
+
+extern "C" mf_status mf_dense_head_f16_ex(const void* hidden, uint64_t hidden_bytes,
+                                          const void* embedding, uint64_t embedding_bytes,
+                                          void* out_keys, uint64_t out_keys_bytes, void* out_ids,
+                                          uint64_t out_ids_bytes, void* out_scores,
+                                          uint64_t out_scores_bytes, void* workspace,
+                                          uint64_t workspace_bytes, uint64_t rows,
+                                          uint64_t hidden_size, uint64_t vocab_rows,
+                                          uint64_t vocab_begin, uint32_t launch_flags,
+                                          void* stream) {
+  return dense_launch(hidden, hidden_bytes, embedding, embedding_bytes, out_keys,
+                      out_keys_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes,
+                      workspace, workspace_bytes, rows, hidden_size, vocab_rows, vocab_begin, 1u,
+                      0u, nullptr, launch_flags, stream);
 }
 
 extern "C" uint64_t mf_exchange_bytes(uint64_t rows, uint32_t world) {
@@ -742,7 +775,7 @@ extern "C" mf_status mf_dense_head_sharded_f16(
     void* out_scores, uint64_t out_scores_bytes, void* workspace, uint64_t workspace_bytes,
     uint64_t rows, uint64_t hidden_size, uint64_t vocab_rows, uint64_t vocab_begin,
     void* const* exchange, uint64_t exchange_bytes, uint32_t world, uint32_t rank,
-    void* stream) {
+    uint32_t launch_flags, void* stream) {
   if (world == 0 || rank >= world || exchange == nullptr) return d_fail(MF_INVALID_ARGUMENT);
   if (world > (uint32_t)kMaxRanks) return d_fail(MF_RESOURCE_LIMIT);
   if (exchange_bytes < mf_exchange_bytes(rows, world)) return d_fail(MF_INVALID_ARGUMENT);
@@ -756,7 +789,7 @@ extern "C" mf_status mf_dense_head_sharded_f16(
   return dense_launch(hidden, hidden_bytes, embedding, embedding_bytes, out_keys,
                       out_keys_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes,
                       workspace, workspace_bytes, rows, hidden_size, vocab_rows, vocab_begin,
-                      world, rank, xbuf, stream);
+                      world, rank, xbuf, launch_flags, stream);
 }
 
 extern "C" mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out_ids,

@@ -136,7 +136,7 @@ Status dense_output_head_sharded_f16(const DeviceBuffer& hidden, const DeviceBuf
       keys.address().valid() ? ma(keys) : nullptr, keys.size_bytes(),
       token_ids.address().valid() ? ma(token_ids) : nullptr, token_ids.size_bytes(), nullptr, 0,
       ma(workspace), workspace.size_bytes(), rows, hidden_size, vocab_rows, vocab_begin, exchange,
-      exchange_bytes, world, rank, st(stream)));
+      exchange_bytes, world, rank, 0u, st(stream)));
 }
 
 }  // namespace marketforge::cuda

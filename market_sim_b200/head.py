@@ -339,6 +339,16 @@ def dense_head_f16(hidden: Buffer, embedding: Buffer, keys: Optional[Buffer],
         *_pb(workspace), rows, hidden_size, vocab_rows, vocab_begin, _sp(stream)))
 
 
+def dense_head_f16_ex(hidden: Buffer, embedding: Buffer, keys: Optional[Buffer],
+                      token_ids: Optional[Buffer], scores: Optional[Buffer], workspace: Buffer,
+                      rows: int, hidden_size: int, vocab_rows: int, vocab_begin: int,
+                      launch_flags: int, stream) -> Status:
+    """``dense_head_f16`` with launch options (``LAUNCH_OVERLAP_PREVIOUS``)."""
+    return _status(lib.mf_dense_head_f16_ex(
+        *_pb(hidden), *_pb(embedding), *_pb(keys), *_pb(token_ids), *_pb(scores),
+        *_pb(workspace), rows, hidden_size, vocab_rows, vocab_begin, launch_flags, _sp(stream)))
+
+
 def decode_keys(keys: Buffer, token_ids: Buffer, scores: Optional[Buffer], rows: int,
                 stream) -> Status:
     """Packed keys (after a cross-shard max) -> ids and scores."""
@@ -357,7 +367,7 @@ def exchange_bytes(rows: int, world: int) -> int:
 def dense_head_sharded_f16(hidden: Buffer, embedding: Buffer, keys: Optional[Buffer],
                            token_ids: Optional[Buffer], scores: Optional[Buffer],
                            workspace: Buffer, rows: int, hidden_size: int, vocab_rows: int,
-                           vocab_begin: int, exchange, stream) -> Status:
+                           vocab_begin: int, exchange, stream, launch_flags: int = 0) -> Status:
     """Vocabulary shards on several GPUs merged inside the dense kernel: every
     rank calls this on its own shard (``vocab_begin`` = the shard's first id)
     and gets the global ids / scores / keys.  ``exchange`` is a
@@ -367,7 +377,7 @@ def dense_head_sharded_f16(hidden: Buffer, embedding: Buffer, keys: Optional[Buf
     return _status(lib.mf_dense_head_sharded_f16(
         *_pb(hidden), *_pb(embedding), *_pb(keys), *_pb(token_ids), *_pb(scores),
         *_pb(workspace), rows, hidden_size, vocab_rows, vocab_begin, arr, exchange.nbytes,
-        exchange.world, exchange.rank, _sp(stream)))
+        exchange.world, exchange.rank, launch_flags, _sp(stream)))
 
 
 class VocabShardExchange:

@@ -271,3 +271,47 @@ def test_dense_sharded_rejects(mf):
     assert call(_Exchange([a.data_ptr(), b.data_ptr()], nb - 8, 2, 0)).code == E.invalid_argument
     assert call(_Exchange([a.data_ptr(), b.data_ptr() + 8], nb, 2, 0)).code == E.invalid_argument
     assert call(_Exchange([a.data_ptr()] * 9, nb, 9, 0)).code == E.resource_limit
+
+
+def test_dense_overlapped_launches_match_plain_calls(mf):
+    """MF_LAUNCH_OVERLAP_PREVIOUS: back-to-back dense launches on independent
+    hidden batches sharing one workspace equal plain calls, eagerly and in a
+    CUDA graph; the workspace is left zero; unknown flag bits are rejected."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    rows, vocab, hs = 512, 8192, 576
+    e_d = to_dev(synth.embedding(95, vocab=vocab))
+    hids = [to_dev(synth.hidden_states(96 + j, rows)) for j in range(4)]
+    want = [_dense(mf, h, e_d, rows, hs, vocab, want_keys=False)[1] for h in hids]
+    ws = torch.zeros(mf.dense_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    outs = [torch.empty(rows, dtype=torch.int32, device="cuda") for _ in hids]
+    s = gpu_stream()
+    flag = mf.LAUNCH_OVERLAP_PREVIOUS
+
+    def launch(j, out):
+        st = mf.dense_head_f16_ex(hids[j], e_d, None, out, None, ws, rows, hs, vocab, 0, flag, s)
+        assert st.ok(), st
+
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            for j in range(len(hids)):
+                launch(j, outs[j])
+    s.synchronize()
+    for o, w in zip(outs, want):
+        assert np.array_equal(o.cpu().numpy().view(np.uint32), w)
+    assert int(ws.sum()) == 0
+    shared = torch.empty(rows, dtype=torch.int32, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for j in (0, 1, 2, 3, 2, 1):
+                launch(j, shared)
+        g.replay()
+        g.replay()
+    s.synchronize()
+    assert np.array_equal(shared.cpu().numpy().view(np.uint32), want[1])
+    assert int(ws.sum()) == 0
+    st = mf.dense_head_f16_ex(hids[0], e_d, None, shared, None, ws, rows, hs, vocab, 0, 4, s)
+    assert st.code == mf.ErrorCode.invalid_argument
