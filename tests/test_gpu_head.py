@@ -520,3 +520,23 @@ def test_overlapped_launches_match_plain_calls(mf, emb_full):
     st = mf.restricted_output_head_csr_f16_ex(h, e_dev, off, ids, *shared, ws, 256, 576, 49_152,
                                               2, s)
     assert st.code == mf.ErrorCode.invalid_argument
+
+    # a malformed batch (decreasing offsets) between good ones: every row of
+    # it gets the sentinel, the workspace is cleared, the next batch is exact
+    bad_off = cases[0][1].copy()
+    assert bad_off[5] > 0
+    bad_off[6] = bad_off[5] - 1  # row 5 ends before it starts
+    bad = to_dev(bad_off)
+    o_bad = (torch.empty(256, dtype=torch.int32, device="cuda"),
+             torch.empty(256, dtype=torch.float32, device="cuda"))
+    with torch.cuda.stream(s):
+        launch(0, *outs[0])
+        st = mf.restricted_output_head_csr_f16_ex(h, e_dev, bad, ids, *o_bad, ws, 256, 576,
+                                                  49_152, flag, s)
+        assert st.ok(), st
+        launch(1, *outs[1])
+    s.synchronize()
+    assert (_u32(o_bad[0]) == INVALID).all()
+    assert np.array_equal(_u32(outs[0][0]), want[0][0])
+    assert np.array_equal(_u32(outs[1][0]), want[1][0])
+    assert int(ws.sum()) == 0
