@@ -161,7 +161,9 @@ def run_ours(args):
         fn = {"dense": lambda: bench_dense(emb, replicas, device, world, rank, stream,
                                            lambda: dist.barrier() if world > 1 else None, identity),
               "decode": lambda: bench_decode(emb, replicas[0], device, rank, stream, identity),
-              "ksweep": lambda: bench_k_sweep(replicas, device, stream)}[args.only]
+              "ksweep": lambda: bench_k_sweep(replicas, device, stream),
+              "rmsnorm": lambda: bench_rmsnorm_fused(batches, replicas, device, stream),
+              "market": lambda: bench_market_decode(emb, replicas[0], device, stream)}[args.only]
         res = fn()
         if rank == 0:
             print(json.dumps({"only": args.only, **res}), flush=True)
@@ -339,6 +341,8 @@ def run_ours(args):
                                             barrier, max_over_ranks),
             "dfa_decode": bench_decode(emb, replicas[0], device, rank, stream, max_over_ranks),
             "k_sweep_batch1": bench_k_sweep(replicas, device, stream),
+            "rmsnorm_fused_head": bench_rmsnorm_fused(batches, replicas, device, stream),
+            "market_dfa_decode": bench_market_decode(emb, replicas[0], device, stream),
         }
         if args.sweep:
             line["secondary"]["k_sweep_batch10k"] = bench_k_sweep(
@@ -595,6 +599,132 @@ def bench_decode(emb, e_dev, device, rank, stream, max_over_ranks, steps=128, ba
             "mean_allowed_set": cand}
 
 
+def bench_rmsnorm_fused(batches, replicas, device, stream, launches=2000):
+    """Fused final RMSNorm + ragged head (``restricted_output_head_csr_rmsnorm_f16``)
+    on the headline batches (B = 256, K log-uniform [1, 4096]) with the last
+    layer's un-normalised rows (N(0, 3) fp16) and an N(1, 0.02) norm weight,
+    against (a) the plain head on rows normalised beforehand and (b) the
+    unfused pair torch rms_norm (fp32, rounded to fp16) + the plain head.
+    Each leg: ``launches`` steps captured in one CUDA graph over rotating
+    batches and embedding copies, events around a replay."""
+    import torch
+
+    from market_sim_b200 import head, synth
+
+    raw = [torch.from_numpy((synth.normal(7000 + j, 1, ROWS * 576) * 3).astype(np.float32)
+                            .astype(np.float16).reshape(ROWS, 576)).to(device)
+           for j in range(len(batches))]
+    gamma = torch.from_numpy(synth.normal(7100, 2, 576, 1.0, 0.02).astype(np.float32)
+                             .astype(np.float16)).to(device)
+    normed = torch.empty((ROWS, 576), dtype=torch.float16, device=device)
+    out = torch.empty(ROWS, dtype=torch.int32, device=device)
+    sc = torch.empty(ROWS, dtype=torch.float32, device=device)
+    ws = torch.zeros(head.head_workspace_bytes(ROWS), dtype=torch.uint8, device=device)
+    h = stream.cuda_stream
+
+    def fused(i):
+        b = batches[i % len(batches)]
+        st = head.restricted_output_head_csr_rmsnorm_f16(
+            raw[i % len(raw)], gamma, 1e-5, replicas[i % len(replicas)], b["off_d"], b["ids_d"],
+            out, sc, ws, ROWS, 576, 49_152, h)
+        if not st.ok():
+            raise RuntimeError(f"fused head failed: {st}")
+
+    def plain(i):
+        b = batches[i % len(batches)]
+        st = head.restricted_output_head_csr_f16(b["hid_d"], replicas[i % len(replicas)],
+                                                 b["off_d"], b["ids_d"], out, sc, ws, ROWS, 576,
+                                                 49_152, h)
+        if not st.ok():
+            raise RuntimeError(f"head failed: {st}")
+
+    def unfused(i):
+        b = batches[i % len(batches)]
+        x = raw[i % len(raw)].float()
+        normed.copy_(torch.nn.functional.rms_norm(x, (576,), gamma.float(), 1e-5))
+        st = head.restricted_output_head_csr_f16(normed, replicas[i % len(replicas)],
+                                                 b["off_d"], b["ids_d"], out, sc, ws, ROWS, 576,
+                                                 49_152, h)
+        if not st.ok():
+            raise RuntimeError(f"head failed: {st}")
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                fn(i)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(launches):
+                    fn(i)
+            g.replay()
+        stream.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            t0.record(stream)
+            g.replay()
+            t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) * 1e3 / launches
+
+    f_us, p_us, u_us = timed(fused), timed(plain), timed(unfused)
+    return {"workload": "headline batches with the final RMSNorm fused in front "
+                        "(un-normalised N(0,3) rows, eps 1e-5)",
+            "fused_us_per_step": f_us, "head_only_us_per_step": p_us,
+            "torch_rms_norm_plus_head_us_per_step": u_us,
+            "fused_seq_per_s": ROWS / (f_us * 1e-6),
+            "timing": "each leg one CUDA graph of the steps (no launch overlap), events "
+                      "around a replay"}
+
+
+def bench_market_decode(emb, e_dev, device, stream, steps=12, batch=256, reps=50):
+    """The reference's SmolLM2 market-action grammar (3,230 states, fan-out
+    <= 11; the fixture tests/golden/market_dfa.npz made from the reference's
+    own DFA) decoded on the device: B sequences from the root state, `steps`
+    steps of allowed-set lookup + head + advance in one CUDA graph."""
+    import torch
+
+    from market_sim_b200 import head, synth
+
+    z = np.load(os.path.join(ROOT, "tests", "golden", "market_dfa.npz"))
+    off, tok, nxt = z["state_offsets"], z["arc_tokens"], z["arc_next"]
+    ns = len(off) - 1
+    hid = torch.from_numpy(synth.decode_hidden(4343, steps, batch)).to(device)
+    off_d = torch.from_numpy(off.astype(np.int32)).to(device)
+    tok_d = torch.from_numpy(tok.astype(np.int32)).to(device)
+    nxt_d = torch.from_numpy(nxt.astype(np.int32)).to(device)
+    trace = torch.zeros((steps + 1, batch), dtype=torch.int32, device=device)
+    tokens = torch.empty((steps, batch), dtype=torch.int32, device=device)
+    ws = torch.zeros(head.dfa_workspace_bytes(batch), dtype=torch.uint8, device=device)
+    h = stream.cuda_stream
+
+    def run():
+        st = head.dfa_decode_f16(hid, e_dev, off_d, tok_d, nxt_d, trace, tokens, None, ws, steps,
+                                 batch, ns, 576, emb.shape[0], h)
+        if not st.ok():
+            raise RuntimeError(f"market decode failed: {st}")
+
+    with torch.cuda.stream(stream):
+        run()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            run()
+        g.replay()
+    stream.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / reps
+    tk = tokens.cpu().numpy().view(np.uint32)
+    return {"workload": f"market-action DFA ({ns} states), B={batch}, {steps} steps from the root "
+                        "in one CUDA graph",
+            "us_per_step": ms * 1e3 / steps, "tokens_per_s": batch * steps / (ms * 1e-3),
+            "emitted_fraction": float((tk != 0xFFFFFFFF).mean())}
+
+
 def cpu_baseline(batch, emb, budget_s=8.0, threads=None):
     """The reference's CPU path timed on this host's cores on a bounded
     sample of the batch's sequences."""
@@ -684,7 +814,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["dense", "decode", "ksweep"],
+    ap.add_argument("--only", choices=["dense", "decode", "ksweep", "rmsnorm", "market"],
                     help="run one secondary workload alone and print its result (profiling)")
     ap.add_argument("--sweep", action="store_true",
                     help="also run the 10k-row K sweep (config 2 throughput; slower to set up)")
