@@ -45,7 +45,7 @@ FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one launch, from one ncu capture of the same
 # workload (profiles/ragged_head_b256_k4096.md, profiles/dense_head_b1024_v49152.md)
 TRAFFIC_RAGGED = 52.50e6
-TRAFFIC_DENSE = 58.02e6
+TRAFFIC_DENSE = 60.47e6
 
 
 def _peaks():
