@@ -602,7 +602,8 @@ static mf_status csr_head(
     const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
     void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
     void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
-    uint64_t vocab, void* stream, const void* gamma, float eps, uint32_t launch_flags) {
+    uint64_t vocab, void* stream, const void* gamma, float eps, uint32_t launch_flags,
+    bool clear_workspace = false) {
   if (rows == 0 || hidden_size == 0 || vocab == 0 || stream == nullptr ||
       (launch_flags & ~MF_LAUNCH_OVERLAP_PREVIOUS) != 0)
     return fail(MF_INVALID_ARGUMENT);
@@ -658,6 +659,12 @@ static mf_status csr_head(
     cfg.numAttrs = 1;
   }
   cudaError_t e;
+  // Allocation-free entry: its shared scratch is cleared only once every
+  // argument has passed, so a rejected call leaves the device untouched.
+  if (clear_workspace) {
+    e = cudaMemsetAsync(workspace, 0, mf_head_workspace_bytes(rows), cfg.stream);
+    if (e != cudaSuccess) return fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+  }
   if (fast && p.gamma)
     e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, true, true>, p, chunk);
   else if (fast)
@@ -889,11 +896,10 @@ extern "C" mf_status mf_head_restricted_csr_f16_noalloc(
   cudaError_t e = noalloc_scratch(&scratch);
   if (e != cudaSuccess) return fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
   const uint64_t bytes = mf_head_workspace_bytes(rows);  // <= MF_NOALLOC_SCRATCH_BYTES
-  // the kernel needs its keys, counters and control words at zero
-  e = cudaMemsetAsync(scratch, 0, bytes, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
-  return mf_head_restricted_csr_f16(hidden, hidden_bytes, embedding, embedding_bytes, offsets,
-                                    offsets_bytes, ids, ids_bytes, out_ids, out_ids_bytes,
-                                    out_scores, out_scores_bytes, scratch, bytes, rows,
-                                    hidden_size, vocab, stream);
+  // csr_head validates every argument first and only then clears the part
+  // of the scratch this call uses (the kernel needs its keys, counters and
+  // control words at zero) before the launch, both on `stream`.
+  return csr_head(hidden, hidden_bytes, embedding, embedding_bytes, offsets, offsets_bytes, ids,
+                  ids_bytes, out_ids, out_ids_bytes, out_scores, out_scores_bytes, scratch, bytes,
+                  rows, hidden_size, vocab, stream, nullptr, 0.f, 0u, true);
 }

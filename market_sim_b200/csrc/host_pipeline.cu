@@ -46,6 +46,22 @@ struct mf_pipeline {
 namespace {
 
 mf_status st_ok() { return mf_status{MF_OK, 0}; }
+
+// Makes the pipeline's device current for the duration of one call and
+// restores the caller's device afterwards (submits launch on the slot
+// streams, which belong to that device).
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceScope(int dev) {
+    err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
+    else if (err == cudaSuccess) prev = -1;  // already current: nothing to restore
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 mf_status st_rt(cudaError_t e) { return mf_status{MF_CUDA_RUNTIME_FAILURE, (uint32_t)e}; }
 
 void release(mf_pipeline* p) {
@@ -139,6 +155,8 @@ extern "C" mf_status mf_pipeline_submit(mf_pipeline* p, const void* hidden, uint
       rows == 0 || (total_ids && ids == nullptr))
     return mf_status{MF_INVALID_ARGUMENT, 0};
   if (rows > p->max_rows || total_ids > p->max_ids) return mf_status{MF_RESOURCE_LIMIT, 0};
+  DeviceScope scope(p->device);
+  if (scope.err != cudaSuccess) return st_rt(scope.err);
   Slot& s = p->slots[p->submitted % p->slots.size()];
   const uint64_t hb = rows * p->hidden_size * 2;
   char* in = static_cast<char*>(s.in);
@@ -160,6 +178,8 @@ extern "C" mf_status mf_pipeline_submit_packed(mf_pipeline* p, const void* batch
     return mf_status{MF_INVALID_ARGUMENT, 0};
   if (rows > p->max_rows || total_ids > p->max_ids) return mf_status{MF_RESOURCE_LIMIT, 0};
   if (batch_bytes != p->packed_bytes(rows, total_ids)) return mf_status{MF_INVALID_ARGUMENT, 0};
+  DeviceScope scope(p->device);
+  if (scope.err != cudaSuccess) return st_rt(scope.err);
   Slot& s = p->slots[p->submitted % p->slots.size()];
   const cudaError_t e =
       cudaMemcpyAsync(s.in, batch, batch_bytes, cudaMemcpyHostToDevice, s.stream);
@@ -170,7 +190,10 @@ extern "C" mf_status mf_pipeline_submit_packed(mf_pipeline* p, const void* batch
 
 extern "C" mf_status mf_pipeline_wait(mf_pipeline* p, uint64_t ticket) {
   if (p == nullptr || ticket >= p->submitted) return mf_status{MF_INVALID_ARGUMENT, 0};
-  if (p->submitted - ticket > p->slots.size()) return st_ok();  // slot reused: already home
+  // The slot's event is re-recorded by every batch that reuses the slot, on
+  // the same stream and after the ticket's own work, so waiting on it also
+  // covers an older ticket whose slot has been reused since (it may wait a
+  // little longer than needed, never less).
   const cudaError_t e = cudaEventSynchronize(p->slots[ticket % p->slots.size()].done);
   return e == cudaSuccess ? st_ok() : st_rt(e);
 }

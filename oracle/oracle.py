@@ -23,12 +23,29 @@ _P = ctypes.c_void_p
 _U64 = ctypes.c_uint64
 
 
+def reference_root():
+    """Where the reference's sources lie: $REF when set, else the
+    `reference_path` recorded in the repository's BASELINE.json; None when
+    neither names an existing directory (e.g. on a GPU box, which only uses
+    the libraries built beforehand)."""
+    path = os.environ.get("REF")
+    if not path:
+        cfg = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+        if os.path.exists(cfg):
+            import json
+
+            with open(cfg) as f:
+                path = json.load(f).get("reference_path")
+    return path if path and os.path.isdir(path) else None
+
+
 def build(ref: bool = False) -> None:
     """Compile the oracle (and the reference CPU library when asked and the
     reference sources are present)."""
     targets = ["all"]
-    if ref and os.path.isdir(os.environ.get("REF", "/root/reference")):
-        targets.append("ref")
+    root = reference_root() if ref else None
+    if root:
+        targets += ["ref", f"REF={root}"]
     subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
 
 

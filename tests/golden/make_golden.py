@@ -184,9 +184,17 @@ def oracle_pin():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None,
+                    help="the reference project's root (default: $REF, else BASELINE.json's "
+                         "reference_path)")
     a = ap.parse_args()
     from oracle import oracle as O
+
+    if a.ref is None:
+        a.ref = O.reference_root()
+    if a.ref is None:
+        ap.error("the reference sources are needed: pass --ref or set REF")
+    os.environ["REF"] = a.ref
 
     O.build(ref=True)
     with open(os.path.join(HERE, "kat_head_3x8x17.json"), "w") as f:
