@@ -65,6 +65,13 @@ struct RaggedParams {
 constexpr int kThreads = 256;
 constexpr int kGroupsPerBlock = kThreads / 8;
 constexpr int kMaxDfaBatch = 8192;
+// CSR batches of up to this many rows are validated by every block on its
+// own (each thread reads at most 16 offsets): a block that finds the offsets
+// malformed gives its share of the rows the sentinel and computes nothing,
+// so no block needs to hear from the others and the kernel ends without a
+// grid-wide arrival counter.  Larger batches keep the counter: the last
+// block out checks a flag the others raised.
+constexpr uint32_t kLocalCheckRows = 16 * kThreads;
 
 // Row-start table for one row mode.  CSR reads global offsets; DFA mode
 // builds the prefix sum of the allowed-set sizes in shared memory.
@@ -174,6 +181,51 @@ __device__ __forceinline__ void rms_norm_fast(const __half* gamma, float eps, in
   }
 }
 
+// Stages hidden row r's 9 chunks owned by this lane into its shared-memory
+// slot (slot[k * kThreads], k = 0..8), normalised first when gamma is set
+// (what rms_norm_f16 would store, as rms_norm_fast).  Two passes over the
+// slot keep at most one row's chunks in registers.
+template <bool kNorm>
+__device__ __forceinline__ void stage_hidden_fast(const __half* hidden, uint32_t r, int sub,
+                                                  unsigned gmask, const __half* gamma, float eps,
+                                                  uint4* slot) {
+  uint4 h[kFastChunksPerLane];
+  load_hidden_fast(hidden, r, sub, h);
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kFastChunksPerLane; ++k) {
+    slot[k * kThreads] = h[k];
+    if (kNorm) {
+      const uint32_t w[4] = {h[k].x, h[k].y, h[k].z, h[k].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+  }
+  if (!kNorm) return;
+  ss = group8_sum(ss, gmask);
+  const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + eps);
+  const uint4* g = reinterpret_cast<const uint4*>(gamma);
+#pragma unroll
+  for (int k = 0; k < kFastChunksPerLane; ++k) {
+    const uint4 gv = ld_v4(g + sub + 8 * k);
+    const uint4 hv = slot[k * kThreads];
+    uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+      const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
+      w[j] = *reinterpret_cast<const uint32_t*>(&o);
+    }
+    slot[k * kThreads] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // inv_rms of hidden row r for the generic path (1 when not normalising).
 __device__ float row_inv_rms(const RaggedParams& p, uint32_t r, int sub, unsigned gmask) {
   if (p.gamma == nullptr) return 1.f;
@@ -202,6 +254,19 @@ __device__ float group_dot_generic(const RaggedParams& p, uint32_t r, uint32_t t
     a = fmaf(hv, __half2float(e[f]), a);
   }
   return group8_sum(a, gmask);
+}
+
+// Row arrival counter: a release-acquire add at GPU scope, so this group's
+// earlier key merge is visible to whichever group completes the row, and the
+// completing group sees every other group's merge (lighter than a full
+// fence around a relaxed add).
+__device__ __forceinline__ uint32_t arrive_acq_rel(uint32_t* counter, uint32_t n) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(counter), "r"(n)
+               : "memory");
+  return old;
 }
 
 // Per-block merge slots: the groups of a block cover one contiguous range of
@@ -248,14 +313,134 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
     }
   }
   if (key != kKeyNone) atomicMax(p.keys + r, key);
-  __threadfence();
-  const uint32_t before = atomicAdd(p.counts + r, (uint32_t)n);
+  const uint32_t before = arrive_acq_rel(p.counts + r, (uint32_t)n);
   if ((int64_t)before + n == row_len) {
-    __threadfence();
     const unsigned long long merged = atomicExch(p.keys + r, 0ull);
     p.counts[r] = 0u;
     finalize_row<M>(p, rows_tab, r, merged);
   }
+}
+
+// 16-byte asynchronous global -> shared copy (no registers on the way) and
+// the wait for every such copy this thread issued.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// One 8-lane group's share of a CSR batch on the 576-wide path: flat
+// candidates [c_begin, c_end).  Each iteration issues the embedding loads of
+// its (up to) two candidates first and only then settles which row they
+// belong to, so the row search at the start and every change of row (the
+// flush of the finished row, the next row's offsets and hidden row) run while
+// those loads are in flight.  The hidden row goes to the lane's shared-memory
+// slot by cp.async (no registers held across the embedding loads); with the
+// fused norm it is normalised in place.  A second candidate that turns out
+// to open the next row is dropped and loaded again by the next iteration.
+template <bool kNorm>
+__device__ __forceinline__ void csr_fast_group(const RaggedParams& p,
+                                               const Rows<RowMode::kCsr>& rows_tab,
+                                               int64_t c_begin, int64_t c_end, int sub,
+                                               unsigned gmask, uint4* slot,
+                                               const BlockSlots& bs) {
+  const uint4* emb = reinterpret_cast<const uint4*>(p.embedding);
+  uint32_t r = 0;
+  int64_t row_b = 0, row_e = c_begin;  // no row yet: the first iteration finds it
+  bool have_row = false;
+  unsigned long long best = kKeyNone;
+  int64_t seen = 0;
+  for (int64_t c = c_begin; c < c_end;) {
+    const bool has1 = c + 1 < c_end;
+    const uint32_t t0 = (uint32_t)__ldg(p.ids + c);
+    const uint32_t t1 = has1 ? (uint32_t)__ldg(p.ids + c + 1) : 0u;
+    const bool v0 = t0 < p.vocab, v1 = has1 && t1 < p.vocab;
+    uint4 e0[kFastChunksPerLane], e1[kFastChunksPerLane];
+    if (v0) {
+      const uint4* row = emb + (size_t)t0 * (kFastHidden / 8) + sub;
+#pragma unroll
+      for (int k = 0; k < kFastChunksPerLane; ++k) e0[k] = ld_stream_v4(row + 8 * k);
+    }
+    if (v1) {
+      const uint4* row = emb + (size_t)t1 * (kFastHidden / 8) + sub;
+#pragma unroll
+      for (int k = 0; k < kFastChunksPerLane; ++k) e1[k] = ld_stream_v4(row + 8 * k);
+    }
+    if (c >= row_e) {
+      if (have_row) {
+        flush_row<RowMode::kCsr>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
+        best = kKeyNone;
+        seen = 0;
+        while (c >= row_e && r + 1 < p.rows) {
+          ++r;
+          row_b = row_e;
+          row_e = rows_tab.at(r + 1);
+        }
+      } else {
+        r = find_row<RowMode::kCsr>(rows_tab, p.rows, c, sub, gmask);
+        row_b = rows_tab.at(r);
+        row_e = rows_tab.at(r + 1);
+        have_row = true;
+      }
+      if (c >= row_e || c < row_b) break;  // malformed offsets: stop
+      const uint4* h = reinterpret_cast<const uint4*>(p.hidden + (size_t)r * kFastHidden) + sub;
+#pragma unroll
+      for (int k = 0; k < kFastChunksPerLane; ++k) cp_async16(slot + k * kThreads, h + 8 * k);
+      cp_async_wait_all();
+      if (kNorm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < kFastChunksPerLane; ++k) {
+          const uint4 hv = slot[k * kThreads];
+          const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            ss = fmaf(f.x, f.x, ss);
+            ss = fmaf(f.y, f.y, ss);
+          }
+        }
+        ss = group8_sum(ss, gmask);
+        const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + p.eps);
+        const uint4* g = reinterpret_cast<const uint4*>(p.gamma) + sub;
+#pragma unroll
+        for (int k = 0; k < kFastChunksPerLane; ++k) {
+          const uint4 gv = ld_v4(g + 8 * k);
+          const uint4 hv = slot[k * kThreads];
+          uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+            const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
+            w[j] = *reinterpret_cast<const uint32_t*>(&o);
+          }
+          slot[k * kThreads] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+    const bool two = has1 && c + 1 < row_e;  // the second candidate is in this row
+    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+#pragma unroll
+    for (int k = 0; k < kFastChunksPerLane; ++k) {
+      const uint4 hk = slot[k * kThreads];
+      if (v0) dot_v4(a00, a01, hk, e0[k]);
+      if (v1) dot_v4(a10, a11, hk, e1[k]);
+    }
+    const float s0 = group8_sum(a00 + a01, gmask);
+    const float s1 = group8_sum(a10 + a11, gmask);
+    best = umax64(best, v0 ? make_key(s0, t0) : kKeyPoison);
+    if (two) best = umax64(best, v1 ? make_key(s1, t1) : kKeyPoison);
+    const int64_t n_here = two ? 2 : 1;
+    seen += n_here;
+    c += n_here;
+  }
+  if (have_row) flush_row<RowMode::kCsr>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
 }
 
 template <RowMode M, bool kFast, bool kNorm = false>
@@ -263,13 +448,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 ragged_head_kernel(RaggedParams p, int64_t chunk) {
   extern __shared__ int32_t smem_rows[];  // DFA mode: rows + 1 starts, then rows arc bases
   __shared__ uint32_t s_last;
-  // Fast path without the fused norm: each lane parks its 9 chunks of the
-  // current hidden row in its own shared-memory slot (strided by thread, so
-  // conflict-free) instead of 36 registers; only that lane reads them, so no
-  // synchronisation.  The freed registers remove the spills of the two
-  // embedding rows in flight (18.7 against 19.5 us per headline batch).
-  constexpr bool kSmemH = kFast && !kNorm;
-  __shared__ uint4 s_hid[kSmemH ? kThreads * kFastChunksPerLane : 1];
+  // Fast path: each lane parks its 9 chunks of the current hidden row (after
+  // the fused norm, when there is one) in its own shared-memory slot
+  // (strided by thread, so conflict-free) instead of 36 registers; only that
+  // lane reads them, so no synchronisation.  The freed registers hold the
+  // two embedding rows in flight without spills (18.7 against 19.5 us per
+  // headline batch for the plain head).
+  __shared__ uint4 s_hid[kFast ? kThreads * kFastChunksPerLane : 1];
 
   Rows<M> rows_tab;
   int64_t total;
@@ -281,6 +466,22 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     pdl_trigger();
     rows_tab.start = p.offsets;
     total = p.total;
+    if (p.rows <= kLocalCheckRows) {
+      int bad = 0;
+      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads)
+        bad |= __ldg(p.offsets + r) > __ldg(p.offsets + r + 1);
+      if (threadIdx.x == 0)
+        bad |= __ldg(p.offsets) != 0 || (int64_t)__ldg(p.offsets + p.rows) != p.total;
+      if (__syncthreads_or(bad)) {  // malformed: sentinel for this block's rows only
+        pdl_wait();
+        for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows;
+             r += gridDim.x * kThreads) {
+          p.out_ids[r] = kInvalid;
+          if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+        }
+        return;
+      }
+    }
   } else {
     pdl_trigger();  // the next decode step's blocks may queue behind this one's
     pdl_wait();     // a decode step reads the states the previous step wrote
@@ -355,24 +556,20 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   const int64_t c_begin = group * chunk;
   const int64_t c_end = min(total, c_begin + chunk);
 
-  if (c_begin < c_end) {
+  if (M == RowMode::kCsr && kFast) {
+    if (c_begin < c_end)
+      csr_fast_group<kNorm>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
+                            c_end, sub, gmask, s_hid + threadIdx.x, bs);
+  } else if (c_begin < c_end) {
     uint32_t r = find_row<M>(rows_tab, p.rows, c_begin, sub, gmask);
     int64_t row_b = rows_tab.at(r);
     int64_t row_e = rows_tab.at(r + 1);
-    const int32_t* cand;  // candidate token ids of the current row, by flat index
-    cand = (M == RowMode::kCsr) ? p.ids : nullptr;
     int64_t arc_base = 0;  // DFA: flat index -> arc index offset
     if constexpr (M == RowMode::kDfa) arc_base = (int64_t)rows_tab.arc_base[r] - row_b;
 
-    uint4 h[kFastChunksPerLane];
     float inv = 1.f;  // generic path: the row's inv_rms when normalising
     if (kFast) {
-      load_hidden_fast(p.hidden, r, sub, h);
-      if (kNorm) rms_norm_fast(p.gamma, p.eps, sub, gmask, h);
-      if (kSmemH) {
-#pragma unroll
-        for (int k = 0; k < kFastChunksPerLane; ++k) s_hid[k * kThreads + threadIdx.x] = h[k];
-      }
+      stage_hidden_fast<kNorm>(p.hidden, r, sub, gmask, p.gamma, p.eps, s_hid + threadIdx.x);
     } else if (kNorm) {
       inv = row_inv_rms(p, r, sub, gmask);
     }
@@ -393,27 +590,24 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
         if (c >= row_e || c < row_b) break;  // malformed offsets: stop
         if constexpr (M == RowMode::kDfa) arc_base = (int64_t)rows_tab.arc_base[r] - row_b;
         if (kFast) {
-          load_hidden_fast(p.hidden, r, sub, h);
-          if (kNorm) rms_norm_fast(p.gamma, p.eps, sub, gmask, h);
-          if (kSmemH) {
-#pragma unroll
-            for (int k = 0; k < kFastChunksPerLane; ++k) s_hid[k * kThreads + threadIdx.x] = h[k];
-          }
+          stage_hidden_fast<kNorm>(p.hidden, r, sub, gmask, p.gamma, p.eps, s_hid + threadIdx.x);
         } else if (kNorm) {
           inv = row_inv_rms(p, r, sub, gmask);
         }
       }
-      // up to two candidates of this row per iteration (one in the fused-norm
-      // variant, whose row-change path needs the registers)
-      constexpr int R = (kNorm && kFast) ? 1 : 2;
+      // up to two candidates of this row per iteration
+      constexpr int R = 2;
       const int64_t n_here = min(min(c_end, row_e) - c, (int64_t)R);
       uint32_t t[R], id[R];
       bool v[R];
 #pragma unroll
       for (int j = 0; j < R; ++j) {
         t[j] = 0;
-        if (j < n_here)
-          t[j] = (M == RowMode::kCsr) ? (uint32_t)cand[c + j] : (uint32_t)p.ids[arc_base + c + j];
+        if constexpr (M == RowMode::kCsr) {
+          if (j < n_here) t[j] = (uint32_t)__ldg(p.ids + c + j);
+        } else if (j < n_here) {
+          t[j] = (uint32_t)p.ids[arc_base + c + j];
+        }
         v[j] = j < n_here && t[j] < p.vocab;
         id[j] = (M == RowMode::kCsr) ? t[j] : (uint32_t)(c + j - row_b);
       }
@@ -433,7 +627,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
         for (int j = 0; j < R; ++j) a[j][0] = a[j][1] = 0.f;
 #pragma unroll
         for (int k = 0; k < kFastChunksPerLane; ++k) {
-          const uint4 hk = kSmemH ? s_hid[k * kThreads + threadIdx.x] : h[k];
+          const uint4 hk = s_hid[k * kThreads + threadIdx.x];
 #pragma unroll
           for (int j = 0; j < R; ++j)
             if (v[j]) dot_v4(a[j][0], a[j][1], hk, e[j][k]);
@@ -455,9 +649,19 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   }
 
   if constexpr (M == RowMode::kDfa) return;
-  // Empty rows get the sentinel here (no group visits them); decreasing
-  // offsets or a bad first/last offset flag the batch.
+  // Empty rows get the sentinel here (no group visits them).
   pdl_wait();
+  if (p.rows <= kLocalCheckRows) {  // offsets checked on entry: no flag, no arrival counter
+    for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += gridDim.x * kThreads) {
+      if (p.offsets[r] == p.offsets[r + 1]) {
+        p.out_ids[r] = kInvalid;
+        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+      }
+    }
+    return;
+  }
+  // Larger batches: decreasing offsets or a bad first/last offset flag the
+  // batch for the last block out.
   for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += gridDim.x * kThreads) {
     const int32_t b = p.offsets[r], e = p.offsets[r + 1];
     if (e < b) {
