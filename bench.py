@@ -43,8 +43,8 @@ REPLICAS = 6
 BATCHES = 8
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one launch, from one ncu capture of the same
-# workload (profiles/ragged_head_b256_k4096.md, profiles/dense_head_b1024_v49152.md)
-TRAFFIC_RAGGED = 52.50e6
+# workload (dram__bytes_read.sum + dram__bytes_write.sum)
+TRAFFIC_RAGGED = 53.95e6
 TRAFFIC_DENSE = 60.47e6
 
 
@@ -184,13 +184,13 @@ def run_ours(args):
         if not st.ok():
             raise RuntimeError(f"head failed: {st}")
 
-    # correctness gate before timing (batch 0 vs the oracle is in the tests;
-    # here: every launch returns a token for every non-empty row)
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             step(i)
     stream.synchronize()
-    assert (out_ids.cpu().numpy().view(np.uint32) != 0xFFFFFFFF).all()
+    # correctness gate before timing: every headline batch through the same
+    # entry point, checked against the CPU oracle under the acceptance rule
+    parity = headline_parity(batches, emb, replicas, out_ids, out_sc, ws, stream, head)
 
     def barrier():
         if world > 1:
@@ -343,12 +343,13 @@ def run_ours(args):
                      "note": "achieved and frac use isolated per-launch events; "
                              "achieved_in_timed_region divides by the per-step time of the "
                              "overlapped graph (algorithmic bytes include rows served by L2)",
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
-                                       "launch (profiles/ragged_head_b256_k4096.md); below the "
-                                       "algorithmic bytes because repeated rows hit in L2"},
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                       "launch of the same batches; below the algorithmic bytes "
+                                       "because repeated rows hit in L2"},
         "e2e": {"value": ROWS * world * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
                 "host_submit_us_per_step": host_submit_s * 1e6 / args.steps},
+        "parity": parity,
         "gpu_launches": args.steps,
         "timing": {"value": "CUDA graph of the K launches (each may overlap the previous "
                             "launch's tail: programmatic dependent launch), events around one "
@@ -357,27 +358,99 @@ def run_ours(args):
                    "e2e": "head.HostPipeline.submit_packed: per step one H2D copy of the "
                           "packed batch (hidden + CSR) from pinned host memory, the head, one "
                           f"D2H copy of ids + scores; {PIPE_DEPTH} slots, copies overlap the "
-                          "other slots' heads; events around K steps"},
+                          "other slots' heads; events around K steps; untimed warm-up covers "
+                          "every pinned batch buffer and slot once"},
         "clocks": clocks.summary(),
     }
     if not args.no_secondary:
         line["secondary"] = {
             "dense_full_vocab": bench_dense(emb, replicas, device, world, rank, stream,
                                             barrier, max_over_ranks),
-            "dfa_decode": bench_decode(emb, replicas[0], device, rank, stream, max_over_ranks),
+            "dfa_decode": bench_decode(emb, replicas[0], device, rank, stream, max_over_ranks,
+                                       cpu=not args.no_cpu),
             "k_sweep_batch1": bench_k_sweep(replicas, device, stream),
+            "k_sweep_batch10k": bench_k_sweep(replicas[:2], device, stream,
+                                              rows_per_launch=10_000, states=1, launches=4),
             "rmsnorm_fused_head": bench_rmsnorm_fused(batches, replicas, device, stream),
             "market_dfa_decode": bench_market_decode(emb, replicas[0], device, stream),
         }
-        if args.sweep:
-            line["secondary"]["k_sweep_batch10k"] = bench_k_sweep(
-                replicas[:2], device, stream, rows_per_launch=10_000, states=2, launches=6)
     if rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(batches[0], emb, budget_s=args.cpu_seconds)
+    if "secondary" in line:
+        line["secondary"] = _slim(line["secondary"])
+        # compact dense (vocabulary-sharded) summary last, where a truncated
+        # tail of the output still holds it
+        d = line["secondary"]["dense_full_vocab"]
+        line["dense_sharded"] = {
+            "n_gpus": world, "rows_per_gpu": 49_152 // world, "ms_per_step": d["ms_per_step"],
+            "kernel_us": d["kernel_us"], "frac": d["roofline"]["frac"],
+            "nccl_merge_ms_per_step": d.get("nccl_merge_ms_per_step"), "parity": d["parity"]}
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def _slim(x):
+    """Floats rounded to 4 significant digits (keeps the one output line short)."""
+    if isinstance(x, dict):
+        return {k: _slim(v) for k, v in x.items()}
+    if isinstance(x, list):
+        return [_slim(v) for v in x]
+    if isinstance(x, float) and x == x and x not in (float("inf"), float("-inf")) and x != 0.0:
+        return float(f"{x:.4g}")
+    return x
+
+
+MARGIN = 1e-3      # ids exact unless the oracle's top-2 margin is below this
+SCORE_RTOL = 2e-3  # scores within this relative tolerance
+
+
+def parity_counts(gpu_ids, gpu_scores, orc_ids, orc_best, orc_ru):
+    """Rows checked, mismatches and margin-exempt rows under the acceptance
+    rule (token ids exact except where the oracle's top-2 margin is below
+    1e-3; scores within 2e-3 relative; sentinel and all-NaN rows exact)."""
+    gpu_ids = np.asarray(gpu_ids).astype(np.uint32)
+    orc_ids = np.asarray(orc_ids).astype(np.uint32)
+    best = np.asarray(orc_best, np.float64)
+    margin = best - np.asarray(orc_ru, np.float64)
+    invalid = orc_ids == 0xFFFFFFFF
+    nan_rows = ~invalid & np.isnan(best)
+    finite = ~invalid & ~nan_rows
+    exempt = finite & (margin < MARGIN)
+    strict = invalid | nan_rows | (finite & ~exempt)
+    bad = strict & (gpu_ids != orc_ids)
+    if gpu_scores is not None:
+        gs = np.asarray(gpu_scores, np.float64)
+        tol = SCORE_RTOL * np.abs(best) + 1e-6
+        bad |= (finite & ~exempt) & ~(np.abs(gs - best) <= tol)
+    return int(gpu_ids.size), int(bad.sum()), int(exempt.sum())
+
+
+def headline_parity(batches, emb, replicas, out_ids, out_sc, ws, stream, head):
+    """The checker leg: each headline batch once through the C-ABI head,
+    compared with the FP32 CPU oracle (oracle/oracle.c, a restatement of the
+    reference CPU path pinned to the reference's own code).  Raises on any
+    mismatch, so no number is reported for a wrong kernel."""
+    from oracle import oracle as O
+
+    rows = mism = exempt = 0
+    for j, b in enumerate(batches):
+        st = head.restricted_output_head_csr_f16(b["hid_d"], replicas[j % len(replicas)],
+                                                 b["off_d"], b["ids_d"], out_ids, out_sc, ws, ROWS,
+                                                 576, 49_152, stream.cuda_stream)
+        if not st.ok():
+            raise RuntimeError(f"head failed: {st}")
+        stream.synchronize()
+        o_ids, o_best, o_ru = O.restricted_head_csr(b["hid"], emb, b["off"], b["ids"],
+                                                    threads=os.cpu_count() or 1)
+        n, m, e = parity_counts(out_ids.cpu().numpy().view(np.uint32), out_sc.cpu().numpy(),
+                                o_ids, o_best, o_ru)
+        rows, mism, exempt = rows + n, mism + m, exempt + e
+    if mism:
+        raise RuntimeError(f"headline parity failed: {mism} of {rows} rows differ from the oracle")
+    return {"batches": len(batches), "rows": rows, "mismatch": mism, "margin_exempt": exempt,
+            "against": "FP32 CPU oracle (restatement of the reference CPU path)"}
 
 
 DENSE_ROWS = 1024
@@ -472,8 +545,44 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
                             per, v0, h)
 
     kms = timed(kernel_only, True)  # the GEMM kernel alone, for the tensor-core roofline
+
+    # parity gate, outside the timed regions: one more step through the same
+    # entry point; every rank's ids must be equal (the in-kernel merge gives
+    # every rank the global answer) and must match a full-vocabulary FP32
+    # argmax of hidden x embedding^T (torch, TF32 off) under the margin rule
+    torch.cuda.synchronize()
+    ids.fill_(-1)
+    with torch.cuda.stream(stream):
+        step(0)
+    stream.synchronize()
+    mine = ids.clone()
+    ranks_equal = True
+    if world > 1:
+        allv = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allv, mine)
+        ranks_equal = all(torch.equal(a, allv[0]) for a in allv)
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    top = (hid.float() @ replicas[0].float().T).topk(2, dim=1)
+    torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+    margin = top.values[:, 0] - top.values[:, 1]
+    strict = margin >= 1e-3
+    mism = int(((mine.long() != top.indices[:, 0]) & strict).sum().item())
+    exempt = int((~strict).sum().item())
+    if world > 1:
+        t = torch.tensor([mism, 0 if ranks_equal else 1], dtype=torch.int64, device=device)
+        dist.all_reduce(t)
+        mism, unequal = int(t[0].item()), int(t[1].item())
+        ranks_equal = unequal == 0
+    del top, margin, strict
     if ex is not None:
         ex.close()
+    if mism or not ranks_equal:
+        raise RuntimeError(f"dense parity failed: {mism} mismatching rows, ranks equal: "
+                           f"{ranks_equal}")
+    parity = {"rows": DENSE_ROWS, "mismatch": mism, "margin_exempt": exempt,
+              "ranks_equal": ranks_equal,
+              "against": "full-vocabulary FP32 argmax of hidden x embedding^T (torch, TF32 off)"}
     flop = 2.0 * DENSE_ROWS * vocab * 576
     peak = _tensor_peak()
     per_gpu_tflops = 2.0 * DENSE_ROWS * per * 576 / (kms * 1e-3) / 1e12
@@ -491,7 +600,7 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
                      "eager_ms_per_step: the same steps launched from Python"
                      + ("; nccl_merge_ms_per_step: kernel + sign flip + NCCL max all-reduce + "
                         "decode, launched from Python" if world > 1 else ""),
-           "eager_ms_per_step": eager_ms}
+           "eager_ms_per_step": eager_ms, "parity": parity}
     if nccl_ms is not None:
         out["nccl_merge_ms_per_step"] = nccl_ms
     return out
@@ -500,35 +609,45 @@ def bench_dense(emb, replicas, device, world, rank, stream, barrier, max_over_ra
 K_SWEEP = (1, 8, 64, 512, 4096, 49_152)
 
 
+def _k_ids(k, rows, seed, device):
+    """rows allowed sets of k distinct ids, uniform over the vocabulary,
+    each row its own set, in random (unsorted) order: the k ids with the
+    largest of 49,152 seeded uniform keys per row (device RNG, chunked)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = torch.empty((rows, k), dtype=torch.int32, device=device)
+    step = max(1, (1 << 28) // 49_152 // 4)  # ~256 MB of keys per chunk
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        keys = torch.rand((r1 - r0, 49_152), generator=g, device=device)
+        out[r0:r1] = keys.topk(k, dim=1).indices.to(torch.int32)
+        del keys
+    return out
+
+
 def bench_k_sweep(replicas, device, stream, rows_per_launch=1, states=16, launches=240):
     """Config 2: allowed-set size K in {1, 8, 64, 512, 4096, 49152}, ids uniform
     without replacement, sorted and unsorted.  rows_per_launch = 1 measures the
-    batch-1 latency (each launch one hidden state); larger values measure
-    throughput.  `states` distinct (hidden, allowed set) states rotate with the
-    embedding copies; launches back to back in one CUDA graph."""
+    batch-1 latency (each launch one hidden state; `states` distinct states
+    rotate); rows_per_launch = 10,000 measures throughput (one launch = 10k
+    hidden states, each with its own allowed set).  Launches back to back in
+    one CUDA graph over rotating embedding copies."""
     import torch
 
     from market_sim_b200 import head, synth
 
     out = {}
     for k in K_SWEEP:
+        draws = [_k_ids(k, rows_per_launch, 70_000 + 131 * k + st, device) for st in range(states)]
+        hid = [torch.from_numpy(synth.hidden_states(70_000 + 131 * k + st, rows_per_launch))
+               .to(device) for st in range(states)]
+        off = torch.from_numpy((np.arange(rows_per_launch + 1, dtype=np.int64) * k)
+                               .astype(np.int32)).to(device)
         for sort_ids in (False, True):
-            hid, offs, idss = [], [], []
-            for st in range(states):
-                seed = 70_000 + 131 * k + st
-                h = synth.hidden_states(seed, rows_per_launch)
-                if k >= 49_152:  # every row allows the whole vocabulary
-                    base = synth.sample_without_replacement(seed, 5, 49_152, 49_152)
-                    ids = np.tile(np.sort(base) if sort_ids else base, rows_per_launch)
-                else:
-                    ids = np.concatenate([
-                        (np.sort(x) if sort_ids else x) for x in
-                        (synth.sample_without_replacement(seed, 10 + r, k, 49_152)
-                         for r in range(rows_per_launch))])
-                off = (np.arange(rows_per_launch + 1, dtype=np.int64) * k).astype(np.int32)
-                hid.append(torch.from_numpy(h).to(device))
-                offs.append(torch.from_numpy(off).to(device))
-                idss.append(torch.from_numpy(ids.astype(np.int32)).to(device))
+            idss = [(d.sort(dim=1).values if sort_ids else d).reshape(-1).contiguous()
+                    for d in draws]
             o_ids = torch.empty(rows_per_launch, dtype=torch.int32, device=device)
             o_sc = torch.empty(rows_per_launch, dtype=torch.float32, device=device)
             ws = torch.zeros(head.head_workspace_bytes(rows_per_launch), dtype=torch.uint8,
@@ -537,8 +656,8 @@ def bench_k_sweep(replicas, device, stream, rows_per_launch=1, states=16, launch
 
             def launch(i):
                 st = head.restricted_output_head_csr_f16(
-                    hid[i % states], replicas[i % len(replicas)], offs[i % states],
-                    idss[i % states], o_ids, o_sc, ws, rows_per_launch, 576, 49_152, hs)
+                    hid[i % states], replicas[i % len(replicas)], off, idss[i % states], o_ids,
+                    o_sc, ws, rows_per_launch, 576, 49_152, hs)
                 if not st.ok():
                     raise RuntimeError(f"k-sweep launch failed: {st}")
 
@@ -557,15 +676,17 @@ def bench_k_sweep(replicas, device, stream, rows_per_launch=1, states=16, launch
                 g.replay()
                 b.record(stream)
             torch.cuda.synchronize()
+            assert (o_ids.cpu().numpy().view(np.uint32) != 0xFFFFFFFF).all()
             us = a.elapsed_time(b) * 1e3 / launches
             alg = rows_per_launch * (k * (1152 + 4) + 1152 + 12) + 4
             out[f"K={k}{',sorted' if sort_ids else ''}"] = {
                 "us_per_launch": round(us, 3),
-                "states_per_s": rows_per_launch / (us * 1e-6),
-                "alg_GBps": alg / (us * 1e-6) / 1e9}
-            del g
+                "states_per_s": round(rows_per_launch / (us * 1e-6)),
+                "alg_GBps": round(alg / (us * 1e-6) / 1e9, 1)}
+            del g, idss
+        del draws, hid
     return {"workload": f"{rows_per_launch} hidden state(s) per launch, K ids uniform without "
-                        f"replacement, {states} rotating states x {len(replicas)} embedding copies",
+                        f"replacement, {states} state set(s) x {len(replicas)} embedding copies",
             "results": out}
 
 
@@ -576,7 +697,8 @@ def _tensor_peak():
     return 1590.0, "fallback"
 
 
-def bench_decode(emb, e_dev, device, rank, stream, max_over_ranks, steps=128, batch=64):
+def bench_decode(emb, e_dev, device, rank, stream, max_over_ranks, steps=128, batch=64,
+                 cpu=True):
     """Config 5: 64-state synthetic DFA, B = 64 sequences x 128 steps of
     allowed-set lookup + restricted head + advance, all on the device, the
     128 steps captured once in a CUDA graph (no host synchronisation)."""
@@ -617,11 +739,41 @@ def bench_decode(emb, e_dev, device, rank, stream, max_over_ranks, steps=128, ba
         t1.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(t0.elapsed_time(t1)) / reps
-    cand = float(np.diff(off).mean())
-    return {"workload": f"64-state DFA, B={batch}, {steps} steps in one CUDA graph",
-            "ms_per_decode": ms, "us_per_step": ms * 1e3 / steps,
-            "tokens_per_s": batch * steps / (ms * 1e-3),
-            "mean_allowed_set": cand}
+    # algorithmic bytes of the decode from its state trace: per step and
+    # sequence the allowed set's embedding rows and ids (K x 1,156 B), the
+    # hidden row (1,152 B), the state in / next state / token (12 B) and the
+    # state's two offsets (8 B)
+    states = trace.cpu().numpy().view(np.uint32)
+    toks = tokens.cpu().numpy().view(np.uint32)
+    sizes = np.diff(off.astype(np.int64))
+    k = sizes[states[:steps].astype(np.int64) % 64]
+    alg = float(k.sum() * 1156 + steps * batch * (1152 + 12 + 8))
+    achieved = alg / (ms * 1e-3) / 1e9
+    hbm_peak, peak_kind = _peaks()
+    out = {"workload": f"64-state DFA, B={batch}, {steps} steps in one CUDA graph",
+           "ms_per_decode": ms, "us_per_step": ms * 1e3 / steps,
+           "tokens_per_s": batch * steps / (ms * 1e-3),
+           "mean_allowed_set": float(k.mean()),
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                        "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                        "algorithmic_bytes_per_step": alg / steps}}
+    if rank == 0 and cpu:
+        # CPU decode baseline: the oracle's decode (the reference CPU head per
+        # step: FP32 dot products of the allowed rows, argmax, DFA advance) on
+        # the first steps, one thread; its tokens must equal the GPU trace
+        from oracle import oracle as O
+
+        cs = 16
+        hid_h = synth.decode_hidden(4242 + rank, steps, batch)[:cs]
+        t = time.perf_counter()
+        o_tok, _ = O.dfa_decode(hid_h, emb, off, tok, 64, states[0], arc_next=nxt)
+        dt = time.perf_counter() - t
+        out["cpu_baseline"] = {"value": batch * cs / dt, "unit": "tokens/s", "cores": 1,
+                               "kind": "port",
+                               "sample": f"{cs} of the {steps} steps, B={batch}, oracle decode "
+                                         "(allowed-row dot products, argmax, advance), 1 thread",
+                               "tokens_equal_gpu": bool(np.array_equal(o_tok, toks[:cs]))}
+    return out
 
 
 def bench_rmsnorm_fused(batches, replicas, device, stream, launches=2000):
@@ -744,42 +896,83 @@ def bench_market_decode(emb, e_dev, device, stream, steps=12, batch=256, reps=50
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / reps
     tk = tokens.cpu().numpy().view(np.uint32)
+    states = trace.cpu().numpy().view(np.uint32)[:steps].astype(np.int64)
+    k = np.diff(off.astype(np.int64))[np.minimum(states, ns - 1)]
+    alg = float(k.sum() * 1156 + steps * batch * (1152 + 12 + 8))
+    achieved = alg / (ms * 1e-3) / 1e9
+    hbm_peak, peak_kind = _peaks()
     return {"workload": f"market-action DFA ({ns} states), B={batch}, {steps} steps from the root "
                         "in one CUDA graph",
             "us_per_step": ms * 1e3 / steps, "tokens_per_s": batch * steps / (ms * 1e-3),
-            "emitted_fraction": float((tk != 0xFFFFFFFF).mean())}
+            "emitted_fraction": float((tk != 0xFFFFFFFF).mean()),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_step": alg / steps}}
+
+
+def _ref_rows(O, kind, batch, emb, emb_f32, rows, threads):
+    """Seconds for the reference CPU path on the first `rows` sequences."""
+    off = batch["off"][: rows + 1]
+    ids = batch["ids"][: off[-1]]
+    hid = batch["hid"][:rows]
+    t = time.perf_counter()
+    if kind == "reference":
+        O.ref_head_csr_by_sequence(hid, emb_f32, off, ids, threads=threads)
+    else:
+        O.full_logits_masked_head_csr(hid, emb, off, ids, threads=threads)
+    return time.perf_counter() - t
 
 
 def cpu_baseline(batch, emb, budget_s=8.0, threads=None):
-    """The reference's CPU path timed on this host's cores on a bounded
-    sample of the batch's sequences."""
+    """The reference's CPU path timed on this host's cores on bounded
+    samples of the batch's sequences: per sequence linear_f32 over all
+    49,152 vocabulary rows + the masked argmax (src/cpu/operators.cpp:539-597,
+    src/cpu/smollm2.cpp:444-462), single-threaded and with the sequences
+    partitioned over every host thread (a reused pool); beside them, the
+    restricted-rows CPU loop (dot products of the allowed rows only, the
+    oracle's C restatement) over the whole batch."""
     from oracle import oracle as O
 
     threads = threads or os.cpu_count() or 1
     kind = "reference" if O.ref_available() else "port"
     emb_f32 = O.widen(emb) if kind == "reference" else None
 
-    def run(rows):
-        off = batch["off"][: rows + 1]
-        ids = batch["ids"][: off[-1]]
-        hid = batch["hid"][:rows]
-        t = time.perf_counter()
-        if kind == "reference":
-            O.ref_full_logits_masked_head_csr(hid, emb_f32, off, ids, threads=threads)
-        else:
-            O.full_logits_masked_head_csr(hid, emb, off, ids, threads=threads)
-        return time.perf_counter() - t
+    def sized(t, share):
+        probe = max(1, min(t, ROWS))
+        dt = _ref_rows(O, kind, batch, emb, emb_f32, probe, t)
+        per_round = max(dt, 1e-3)  # one sequence per thread
+        rounds = max(1, int(budget_s * share / per_round))
+        rows = int(min(ROWS, probe * rounds))
+        dt = _ref_rows(O, kind, batch, emb, emb_f32, rows, t) if rows > probe else dt
+        return rows, dt
 
-    probe = min(threads, ROWS)
-    dt = run(probe)
-    rows = int(min(ROWS, max(probe, probe * max(1, int(budget_s / max(dt, 1e-3))))))
-    dt = run(rows) if rows > probe else dt
-    return {"value": rows / dt, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{rows} of the batch's 256 sequences; per sequence linear_f32 over all "
-                      f"49152 vocab rows + masked argmax, {threads} threads"}
+    rows1, dt1 = sized(1, 0.3)
+    rows_n, dt_n = sized(threads, 0.6)
+    t = time.perf_counter()
+    O.restricted_head_csr(batch["hid"], emb, batch["off"], batch["ids"], threads=threads)
+    dt_r = time.perf_counter() - t
+    what = "per sequence linear_f32 over all 49152 vocab rows + masked argmax"
+    return {"value": rows_n / dt_n, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{rows_n} of a batch's 256 sequences, {what}, sequences split over "
+                      f"{threads} threads",
+            "single_thread": {"value": rows1 / dt1, "unit": UNIT, "cores": 1, "kind": kind,
+                              "sample": f"{rows1} sequences, {what}, 1 thread"},
+            "n_threads": {"value": rows_n / dt_n, "unit": UNIT, "cores": threads, "kind": kind,
+                          "sample": f"{rows_n} sequences, {what}, {threads} threads"},
+            "restricted_rows": {"value": ROWS / dt_r, "unit": UNIT, "cores": threads,
+                                "kind": "port",
+                                "sample": "the whole 256-sequence batch, dot products of the "
+                                          "allowed rows only (oracle C restatement of the "
+                                          f"reference arithmetic), {threads} threads"}}
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU path (oracle/_ref, built
+    from the reference's sources; the oracle's C restatement only where
+    _ref is absent) on the host cores, the batch's sequences partitioned over
+    all host threads of a reused pool.  One step = a bounded sample of
+    2 x threads sequences (two per thread), rotating through the
+    256-sequence headline batch, so any --steps stays within minutes."""
     world, rank, _ = _dist()
     if rank != 0:
         return
@@ -793,27 +986,25 @@ def run_reference(args):
     seed = 10_000
     hid = synth.hidden_states(seed, ROWS)
     off, ids = synth.ragged_batch(seed, rows=ROWS, kmax=KMAX)
-    # one sequence per step (rotating through the batch), its 49,152 logits
-    # split over all host threads by vocabulary slices, so K steps stay
-    # within a few minutes for the step counts the driver uses
-    per_step = 1
+    per_step = min(ROWS, 2 * threads)
 
     def step(i):
-        r0 = i % ROWS
-        o = (off[r0:r0 + 2] - off[r0]).astype(np.int32)
-        sel = ids[off[r0]:off[r0 + 1]]
+        r0 = (i * per_step) % ROWS
+        rows = min(per_step, ROWS - r0)
+        o = (off[r0:r0 + rows + 1] - off[r0]).astype(np.int32)
+        sel = ids[off[r0]:off[r0 + rows]]
         if kind == "reference":
-            O.ref_full_logits_masked_head_csr(hid[r0:r0 + 1], emb_f32, o, sel, threads=threads)
+            O.ref_head_csr_by_sequence(hid[r0:r0 + rows], emb_f32, o, sel, threads=threads)
         else:
-            O.full_logits_masked_head_csr(hid[r0:r0 + 1], emb, o, sel, threads=1)
+            O.full_logits_masked_head_csr(hid[r0:r0 + rows], emb, o, sel, threads=threads)
+        return rows
 
     for i in range(args.warmup):
         step(i)
     t = time.perf_counter()
-    for i in range(args.steps):
-        step(args.warmup + i)
+    done = sum(step(args.warmup + i) for i in range(args.steps))
     dt = time.perf_counter() - t
-    value = per_step * args.steps / dt
+    value = done / dt
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
@@ -822,12 +1013,11 @@ def run_reference(args):
         "config": {"workload": "ragged restricted head, B=256 per GPU, K log-uniform [1,4096], "
                                "CSR int32, hidden 576, vocab 49152",
                    "global_batch": ROWS * world, "parallelism": "host CPU"},
-        "cpu_baseline": {"value": value, "unit": UNIT,
-                         "cores": threads if kind == "reference" else 1, "kind": kind,
-                         "sample": "one sequence per step, rotating through a 256-sequence "
-                                   "ragged batch; reference linear_f32 over all 49152 vocab "
-                                   "rows (split over the host threads by vocabulary slice) + "
-                                   "masked argmax"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{per_step} sequences per step (two per thread), rotating "
+                                   "through a 256-sequence ragged batch; reference linear_f32 "
+                                   "over all 49152 vocab rows + masked argmax per sequence, "
+                                   f"sequences split over {threads} threads of a reused pool"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -841,8 +1031,6 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--only", choices=["dense", "decode", "ksweep", "rmsnorm", "market"],
                     help="run one secondary workload alone and print its result (profiling)")
-    ap.add_argument("--sweep", action="store_true",
-                    help="also run the 10k-row K sweep (config 2 throughput; slower to set up)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the dense full-vocab and DFA-decode measurements")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

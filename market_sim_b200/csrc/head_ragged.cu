@@ -145,46 +145,12 @@ __device__ __forceinline__ void load_hidden_fast(const __half* hidden, uint32_t 
   for (int k = 0; k < kFastChunksPerLane; ++k) h[k] = ld_v4(row + sub + 8 * k);
 }
 
-// Fused final RMSNorm of the row held in h (fast path): what the reference's
-// rms_norm_f16 (src/cuda/rms_norm.cu:69-100) would store, computed in FP32
-// and rounded to fp16: inv = 1 / sqrt(mean(x^2) + eps), h = fp16(x * inv * w)
-// (the order of src/cpu/operators.cpp:522-535).
-__device__ __forceinline__ void rms_norm_fast(const __half* gamma, float eps, int sub,
-                                              unsigned gmask, uint4 (&h)[kFastChunksPerLane]) {
-  float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < kFastChunksPerLane; ++k) {
-    const uint32_t w[4] = {h[k].x, h[k].y, h[k].z, h[k].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-      ss = fmaf(f.x, f.x, ss);
-      ss = fmaf(f.y, f.y, ss);
-    }
-  }
-  ss = group8_sum(ss, gmask);
-  const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + eps);
-  const uint4* g = reinterpret_cast<const uint4*>(gamma);
-#pragma unroll
-  for (int k = 0; k < kFastChunksPerLane; ++k) {
-    const uint4 gv = ld_v4(g + sub + 8 * k);
-    uint32_t w[4] = {h[k].x, h[k].y, h[k].z, h[k].w};
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
-      const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
-      w[j] = *reinterpret_cast<const uint32_t*>(&o);
-    }
-    h[k] = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
-
 // Stages hidden row r's 9 chunks owned by this lane into its shared-memory
 // slot (slot[k * kThreads], k = 0..8), normalised first when gamma is set
-// (what rms_norm_f16 would store, as rms_norm_fast).  Two passes over the
-// slot keep at most one row's chunks in registers.
+// (what the reference's rms_norm_f16, src/cuda/rms_norm.cu:69-100, would
+// store: inv = 1 / sqrt(mean(x^2) + eps) in FP32, h = fp16(x * inv * w), the
+// order of src/cpu/operators.cpp:522-535).  Two passes over the slot keep at
+// most one row's chunks in registers.
 template <bool kNorm>
 __device__ __forceinline__ void stage_hidden_fast(const __half* hidden, uint32_t r, int sub,
                                                   unsigned gmask, const __half* gamma, float eps,
@@ -333,33 +299,110 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// One 8-lane group's share of a CSR batch on the 576-wide path: flat
-// candidates [c_begin, c_end).  Each iteration issues the embedding loads of
-// its (up to) two candidates first and only then settles which row they
-// belong to, so the row search at the start and every change of row (the
-// flush of the finished row, the next row's offsets and hidden row) run while
-// those loads are in flight.  The hidden row goes to the lane's shared-memory
-// slot by cp.async (no registers held across the embedding loads); with the
-// fused norm it is normalised in place.  A second candidate that turns out
-// to open the next row is dropped and loaded again by the next iteration.
+// Rows a thread block can stage once for all its groups (the block's
+// candidate range covers at most this many rows); blocks spanning more rows
+// stage per group.
+constexpr int kBlockRows = 16;
+// Dynamic shared memory of the CSR fast path: the per-lane hidden slots and
+// the block's row table.
+constexpr int kCsrFastSmem = (kThreads * kFastChunksPerLane + kBlockRows * 72) * 16;
+
+// Shared-memory row table of a block on the CSR fast path.
+struct BlockRowTable {
+  uint4* rows;     // [kBlockRows][72] hidden rows (normalised when fusing the norm)
+  int64_t* start;  // [kBlockRows + 1] offsets of rows first .. first + n
+  uint32_t first;  // first row of the block's candidate range
+  int n;           // rows staged (0: the block stages per group)
+};
+
+// Warp-cooperative staging of hidden row r into dst (72 x 16 B): lane l
+// owns chunks l, l + 32, l + 64 (< 72).  With the fused norm the row is
+// normalised as the reference's rms_norm_f16 would store it
+// (src/cuda/rms_norm.cu:69-100: inv = 1 / sqrt(mean(x^2) + eps) in FP32,
+// h = fp16(x * inv * w), the order of src/cpu/operators.cpp:522-535).
 template <bool kNorm>
-__device__ __forceinline__ void csr_fast_group(const RaggedParams& p,
+__device__ __forceinline__ void stage_row_warp(const RaggedParams& p, uint32_t r, uint4* dst,
+                                               int lane) {
+  const uint4* src = reinterpret_cast<const uint4*>(p.hidden + (size_t)r * kFastHidden);
+  uint4 v[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int ch = lane + 32 * j;
+    v[j] = ch < 72 ? ld_v4(src + ch) : make_uint4(0, 0, 0, 0);
+  }
+  if (kNorm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[q]));
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + p.eps);
+    const uint4* g = reinterpret_cast<const uint4*>(p.gamma);
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int ch = lane + 32 * j;
+      if (ch >= 72) continue;
+      const uint4 gv = ld_v4(g + ch);
+      uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[q]));
+        const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[q]));
+        const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
+        w[q] = *reinterpret_cast<const uint32_t*>(&o);
+      }
+      v[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+    if (lane + 32 * j < 72) dst[lane + 32 * j] = v[j];
+}
+
+// The CSR fast path (576-wide rows) for a whole thread block; every thread
+// calls it (it holds block barriers).  Group g of the block owns flat
+// candidates [c_begin, c_end).
+//   * Each group issues the embedding loads of its first two candidates at
+//     once; while they are in flight the block finds the rows its range
+//     covers and, when they are at most kBlockRows, stages those hidden rows
+//     (normalised, when fusing the norm) and their offsets in shared memory
+//     once for all groups, a warp per row.
+//   * Each iteration then issues the embedding loads of its (up to) two
+//     candidates before settling which row they belong to, so a change of
+//     row (the flush of the finished row, the next row's offsets and hidden
+//     row) runs while those loads are in flight.  A second candidate that
+//     turns out to open the next row is dropped and loaded again by the next
+//     iteration.
+//   * A block spanning more rows (many short rows) stages per group: the
+//     lane's own shared-memory slot by cp.async, normalised in place.
+template <bool kNorm>
+__device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
                                                const Rows<RowMode::kCsr>& rows_tab,
                                                int64_t c_begin, int64_t c_end, int sub,
                                                unsigned gmask, uint4* slot,
-                                               const BlockSlots& bs) {
+                                               const BlockSlots& bs, BlockRowTable& tab,
+                                               uint32_t* s_rows_found) {
   const uint4* emb = reinterpret_cast<const uint4*>(p.embedding);
-  uint32_t r = 0;
-  int64_t row_b = 0, row_e = c_begin;  // no row yet: the first iteration finds it
-  bool have_row = false;
-  unsigned long long best = kKeyNone;
-  int64_t seen = 0;
-  for (int64_t c = c_begin; c < c_end;) {
-    const bool has1 = c + 1 < c_end;
-    const uint32_t t0 = (uint32_t)__ldg(p.ids + c);
-    const uint32_t t1 = has1 ? (uint32_t)__ldg(p.ids + c + 1) : 0u;
-    const bool v0 = t0 < p.vocab, v1 = has1 && t1 < p.vocab;
-    uint4 e0[kFastChunksPerLane], e1[kFastChunksPerLane];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int64_t c = c_begin;
+  uint32_t t0 = 0, t1 = 0;
+  bool has1 = false, v0 = false, v1 = false;
+  uint4 e0[kFastChunksPerLane], e1[kFastChunksPerLane];
+  auto issue = [&]() {
+    has1 = c + 1 < c_end;
+    t0 = (uint32_t)__ldg(p.ids + c);
+    t1 = has1 ? (uint32_t)__ldg(p.ids + c + 1) : 0u;
+    v0 = t0 < p.vocab;
+    v1 = has1 && t1 < p.vocab;
     if (v0) {
       const uint4* row = emb + (size_t)t0 * (kFastHidden / 8) + sub;
 #pragma unroll
@@ -370,65 +413,124 @@ __device__ __forceinline__ void csr_fast_group(const RaggedParams& p,
 #pragma unroll
       for (int k = 0; k < kFastChunksPerLane; ++k) e1[k] = ld_stream_v4(row + 8 * k);
     }
-    if (c >= row_e) {
-      if (have_row) {
-        flush_row<RowMode::kCsr>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
-        best = kKeyNone;
-        seen = 0;
-        while (c >= row_e && r + 1 < p.rows) {
-          ++r;
-          row_b = row_e;
-          row_e = rows_tab.at(r + 1);
-        }
+  };
+  if (c < c_end) issue();
+
+  // ---- the block's rows: [first, last] covering [bs.begin, bs.end) ----
+  if (warp == 0 && lane < 16) {  // group 0: first row, group 1: last row
+    const int64_t at = lane < 8 ? bs.begin : bs.end - 1;
+    uint32_t r = 0;
+    if (bs.begin < bs.end) r = find_row<RowMode::kCsr>(rows_tab, p.rows, at, sub, gmask);
+    if (sub == 0) s_rows_found[lane >> 3] = r;
+  }
+  __syncthreads();
+  const uint32_t first = s_rows_found[0], last = s_rows_found[1];
+  const int64_t span = (int64_t)last - (int64_t)first + 1;
+  tab.first = first;
+  tab.n = (bs.begin < bs.end && span >= 1 && span <= kBlockRows) ? (int)span : 0;
+  if (tab.n > 0) {
+    for (int i = warp; i < tab.n; i += kThreads / 32)
+      stage_row_warp<kNorm>(p, first + (uint32_t)i, tab.rows + i * 72, lane);
+    if ((int)threadIdx.x <= tab.n) tab.start[threadIdx.x] = rows_tab.at(first + threadIdx.x);
+  }
+  __syncthreads();
+
+  // ---- the group's candidates ----
+  const bool table = tab.n > 0;
+  const uint4* hid = slot;  // current hidden row: chunk k at hid[k * hstride]
+  const int hstride = table ? 8 : kThreads;
+  uint32_t r = 0;
+  int64_t row_b = 0, row_e = c_begin;  // no row yet: the first iteration finds it
+  bool have_row = false, pre = true;
+  unsigned long long best = kKeyNone;
+  int64_t seen = 0;
+  auto row_start = [&](uint32_t q) -> int64_t {
+    return table ? tab.start[q - first] : rows_tab.at(q);
+  };
+  // Row change: flush the finished row, find the next one, point at (or
+  // stage) its hidden state.  false: malformed offsets (stop).
+  auto enter_row = [&]() -> bool {
+    const uint32_t r_end = table ? first + (uint32_t)tab.n : p.rows;  // rows [.., r_end)
+    if (have_row) {
+      flush_row<RowMode::kCsr>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
+      best = kKeyNone;
+      seen = 0;
+      while (c >= row_e && r + 1 < r_end) {
+        ++r;
+        row_b = row_e;
+        row_e = row_start(r + 1);
+      }
+    } else {
+      if (table) {
+        r = first;
+        while (r + 1 < r_end && tab.start[r + 1 - first] <= c) ++r;
       } else {
         r = find_row<RowMode::kCsr>(rows_tab, p.rows, c, sub, gmask);
-        row_b = rows_tab.at(r);
-        row_e = rows_tab.at(r + 1);
-        have_row = true;
       }
-      if (c >= row_e || c < row_b) break;  // malformed offsets: stop
-      const uint4* h = reinterpret_cast<const uint4*>(p.hidden + (size_t)r * kFastHidden) + sub;
+      row_b = row_start(r);
+      row_e = row_start(r + 1);
+      have_row = true;
+    }
+    if (c >= row_e || c < row_b) return false;  // malformed offsets: stop
+    if (table) {
+      hid = tab.rows + (r - first) * 72 + sub;
+      return true;
+    }
+    const uint4* h = reinterpret_cast<const uint4*>(p.hidden + (size_t)r * kFastHidden) + sub;
 #pragma unroll
-      for (int k = 0; k < kFastChunksPerLane; ++k) cp_async16(slot + k * kThreads, h + 8 * k);
-      cp_async_wait_all();
-      if (kNorm) {
-        float ss = 0.f;
+    for (int k = 0; k < kFastChunksPerLane; ++k) cp_async16(slot + k * kThreads, h + 8 * k);
+    cp_async_wait_all();
+    if (kNorm) {
+      float ss = 0.f;
 #pragma unroll
-        for (int k = 0; k < kFastChunksPerLane; ++k) {
-          const uint4 hv = slot[k * kThreads];
-          const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+      for (int k = 0; k < kFastChunksPerLane; ++k) {
+        const uint4 hv = slot[k * kThreads];
+        const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-            ss = fmaf(f.x, f.x, ss);
-            ss = fmaf(f.y, f.y, ss);
-          }
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+          ss = fmaf(f.x, f.x, ss);
+          ss = fmaf(f.y, f.y, ss);
         }
-        ss = group8_sum(ss, gmask);
-        const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + p.eps);
-        const uint4* g = reinterpret_cast<const uint4*>(p.gamma) + sub;
+      }
+      ss = group8_sum(ss, gmask);
+      const float inv = 1.0f / sqrtf(ss / (float)kFastHidden + p.eps);
+      const uint4* g = reinterpret_cast<const uint4*>(p.gamma) + sub;
 #pragma unroll
-        for (int k = 0; k < kFastChunksPerLane; ++k) {
-          const uint4 gv = ld_v4(g + 8 * k);
-          const uint4 hv = slot[k * kThreads];
-          uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      for (int k = 0; k < kFastChunksPerLane; ++k) {
+        const uint4 gv = ld_v4(g + 8 * k);
+        const uint4 hv = slot[k * kThreads];
+        uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-            const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
-            const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
-            w[j] = *reinterpret_cast<const uint32_t*>(&o);
-          }
-          slot[k * kThreads] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+          const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+          const __half2 o = __floats2half2_rn(x.x * inv * y.x, x.y * inv * y.y);
+          w[j] = *reinterpret_cast<const uint32_t*>(&o);
         }
+        slot[k * kThreads] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
+    hid = slot;
+    return true;
+  };
+
+  while (c < c_end) {
+    if (!pre) {
+      // the per-group fallback with the fused norm enters a new row before
+      // issuing the loads: the normalisation needs registers that two rows in
+      // flight would occupy
+      if (kNorm && !table && c >= row_e && !enter_row()) break;
+      issue();
+    }
+    pre = false;
+    if (c >= row_e && !enter_row()) break;
     const bool two = has1 && c + 1 < row_e;  // the second candidate is in this row
     float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
 #pragma unroll
     for (int k = 0; k < kFastChunksPerLane; ++k) {
-      const uint4 hk = slot[k * kThreads];
+      const uint4 hk = hid[k * hstride];
       if (v0) dot_v4(a00, a01, hk, e0[k]);
       if (v1) dot_v4(a10, a11, hk, e1[k]);
     }
@@ -446,7 +548,10 @@ __device__ __forceinline__ void csr_fast_group(const RaggedParams& p,
 template <RowMode M, bool kFast, bool kNorm = false>
 __global__ void __launch_bounds__(kThreads, 2)
 ragged_head_kernel(RaggedParams p, int64_t chunk) {
-  extern __shared__ int32_t smem_rows[];  // DFA mode: rows + 1 starts, then rows arc bases
+  // Dynamic shared memory: DFA mode, rows + 1 starts then rows arc bases;
+  // CSR fast path, the per-lane hidden slots then the block's row table
+  // (kCsrFastSmem bytes).
+  extern __shared__ __align__(16) int32_t smem_rows[];
   __shared__ uint32_t s_last;
   // Fast path: each lane parks its 9 chunks of the current hidden row (after
   // the fused norm, when there is one) in its own shared-memory slot
@@ -454,7 +559,8 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   // lane reads them, so no synchronisation.  The freed registers hold the
   // two embedding rows in flight without spills (18.7 against 19.5 us per
   // headline batch for the plain head).
-  __shared__ uint4 s_hid[kFast ? kThreads * kFastChunksPerLane : 1];
+  __shared__ uint4 s_hid_dfa[(kFast && M == RowMode::kDfa) ? kThreads * kFastChunksPerLane : 1];
+  uint4* const s_hid = M == RowMode::kCsr ? reinterpret_cast<uint4*>(smem_rows) : s_hid_dfa;
 
   Rows<M> rows_tab;
   int64_t total;
@@ -557,9 +663,13 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   const int64_t c_end = min(total, c_begin + chunk);
 
   if (M == RowMode::kCsr && kFast) {
-    if (c_begin < c_end)
-      csr_fast_group<kNorm>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
-                            c_end, sub, gmask, s_hid + threadIdx.x, bs);
+    __shared__ uint32_t s_rows_found[2];
+    __shared__ int64_t s_tab_start[kBlockRows + 1];
+    BlockRowTable tab;
+    tab.rows = s_hid + kThreads * kFastChunksPerLane;  // after the per-lane slots
+    tab.start = s_tab_start;
+    csr_fast_block<kNorm>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
+                          c_end, sub, gmask, s_hid + threadIdx.x, bs, tab, s_rows_found);
   } else if (c_begin < c_end) {
     uint32_t r = find_row<M>(rows_tab, p.rows, c_begin, sub, gmask);
     int64_t row_b = rows_tab.at(r);
@@ -725,8 +835,12 @@ static DeviceInfo& device_info() {
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
         &d.blocks_per_sm[0][0], ragged_head_kernel<RowMode::kCsr, false>, kThreads, 0);
+    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kCsr, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, kCsrFastSmem);
+    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kCsr, true, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, kCsrFastSmem);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &d.blocks_per_sm[0][1], ragged_head_kernel<RowMode::kCsr, true>, kThreads, 0);
+        &d.blocks_per_sm[0][1], ragged_head_kernel<RowMode::kCsr, true>, kThreads, kCsrFastSmem);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
         &d.blocks_per_sm[1][0], ragged_head_kernel<RowMode::kDfa, false>, kThreads, 4096);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
@@ -854,6 +968,7 @@ static mf_status csr_head(
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = fast ? kCsrFastSmem : 0;
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   if (launch_flags & MF_LAUNCH_OVERLAP_PREVIOUS) {

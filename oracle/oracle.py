@@ -219,11 +219,13 @@ def ref_lib():
         r.mfref_linear_f32.argtypes = [_P, _P, _U64, _U64, _U64, _P]
         r.mfref_full_logits_masked_head_csr.argtypes = [_P, _P, _P, _P, _U64, _U64, _U64, _P, _P,
                                                         ctypes.c_int]
+        r.mfref_head_csr_by_sequence.argtypes = [_P, _P, _P, _P, _U64, _U64, _U64, _P, _P,
+                                                 ctypes.c_int]
         r.mfref_market_dfa.argtypes = [_P, _P, _P, _P, _P, _P]
         r.mfref_market_dfa_advance.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
         r.mfref_market_dfa_advance.restype = ctypes.c_uint32
         for f in ("mfref_rms_norm_f32", "mfref_linear_f32", "mfref_full_logits_masked_head_csr",
-                  "mfref_market_dfa"):
+                  "mfref_head_csr_by_sequence", "mfref_market_dfa"):
             getattr(r, f).restype = ctypes.c_int
         _ref = r
     return _ref
@@ -256,6 +258,24 @@ def ref_full_logits_masked_head_csr(hidden_f16, emb_f32, offsets, ids, threads=1
     out = np.empty(rows, np.uint32)
     best = np.empty(rows, np.float32)
     code = ref_lib().mfref_full_logits_masked_head_csr(
+        _p(hidden), _p(emb_f32), _p(offsets), _p(ids), rows, hidden.shape[1], emb_f32.shape[0],
+        _p(out), _p(best), threads)
+    assert code == 0, code
+    return out, best
+
+
+def ref_head_csr_by_sequence(hidden_f16, emb_f32, offsets, ids, threads=1):
+    """The reference CPU path (linear_f32 over every vocab row, masked
+    argmax) with the batch's sequences split over `threads` threads of a
+    pool that persists between calls.  -> (ids u32[rows], best f32[rows])."""
+    hidden = widen(hidden_f16)
+    emb_f32 = np.ascontiguousarray(emb_f32, np.float32)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    rows = hidden.shape[0]
+    out = np.empty(rows, np.uint32)
+    best = np.empty(rows, np.float32)
+    code = ref_lib().mfref_head_csr_by_sequence(
         _p(hidden), _p(emb_f32), _p(offsets), _p(ids), rows, hidden.shape[1], emb_f32.shape[0],
         _p(out), _p(best), threads)
     assert code == 0, code

@@ -7,9 +7,12 @@
 // mfref_full_logits_masked_head_csr on the host cores.  Nothing in the
 // product links or loads it.
 #include <cmath>
+#include <condition_variable>
 #include <cstdint>
 #include <cstring>
+#include <functional>
 #include <limits>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -140,6 +143,115 @@ int mfref_full_logits_masked_head_csr(const float* hidden, const float* embeddin
   for (int t = 1; t < threads; ++t) pool.emplace_back(work, t);
   work(0);
   for (auto& th : pool) th.join();
+  for (int c : codes)
+    if (c != 0) return c;
+  return 0;
+}
+
+} // extern "C"
+
+namespace {
+
+// A fixed set of worker threads reused across calls (the benchmark's
+// reference arm calls once per step; spawning threads per call would be
+// timed with the work).  run(f) executes f(0..n-1) with f(0) on the caller.
+class Pool {
+ public:
+  void ensure(int n) {
+    if (n == size_) return;
+    stop();
+    size_ = n;
+    const std::uint64_t now = gen_;  // new workers wait for the next job, not a past one
+    for (int t = 1; t < n; ++t) workers_.emplace_back([this, t, now] { loop(t, now); });
+  }
+  void run(const std::function<void(int)>& f) {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      job_ = &f;
+      pending_ = size_ - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    f(0);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [this] { return pending_ == 0; });
+    job_ = nullptr;
+  }
+  ~Pool() { stop(); }
+
+ private:
+  void loop(int t, std::uint64_t seen) {
+    for (;;) {
+      const std::function<void(int)>* f;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return quit_ || gen_ != seen; });
+        if (quit_) return;
+        seen = gen_;
+        f = job_;
+      }
+      (*f)(t);
+      std::lock_guard<std::mutex> lk(mu_);
+      if (--pending_ == 0) done_.notify_one();
+    }
+  }
+  void stop() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      quit_ = true;
+    }
+    cv_.notify_all();
+    for (auto& w : workers_) w.join();
+    workers_.clear();
+    quit_ = false;
+    size_ = 1;
+  }
+  std::mutex mu_;
+  std::condition_variable cv_, done_;
+  std::vector<std::thread> workers_;
+  const std::function<void(int)>* job_ = nullptr;
+  std::uint64_t gen_ = 0;
+  int pending_ = 0, size_ = 1;
+  bool quit_ = false;
+};
+
+Pool& pool() {
+  static Pool p;
+  return p;
+}
+
+} // namespace
+
+extern "C" {
+
+// The reference CPU path for a ragged batch with sequences partitioned over
+// `threads` host threads of a reused pool: each thread takes a contiguous
+// range of rows and, per row, runs linear_f32 over every vocab row of the
+// FP32 embedding, then the masked argmax over the row's CSR candidates.
+int mfref_head_csr_by_sequence(const float* hidden, const float* embedding_f32,
+                               const std::int32_t* offsets, const std::int32_t* ids,
+                               std::uint64_t rows, std::uint64_t hidden_size,
+                               std::uint64_t vocab, std::uint32_t* out_ids, float* out_best,
+                               int threads) {
+  if (threads < 1) threads = 1;
+  pool().ensure(threads);
+  std::vector<int> codes(static_cast<std::size_t>(threads), 0);
+  const std::function<void(int)> work = [&](int t) {
+    thread_local std::vector<float> logits;
+    logits.resize(vocab);
+    const std::uint64_t b = rows * t / threads, e = rows * (t + 1) / threads;
+    for (std::uint64_t r = b; r < e; ++r) {
+      const int code = mfref_linear_f32(hidden + r * hidden_size, embedding_f32, 1, hidden_size,
+                                        vocab, logits.data());
+      if (code != 0) {
+        codes[t] = code;
+        return;
+      }
+      masked_pick(logits.data(), ids + offsets[r], offsets[r + 1] - offsets[r], vocab,
+                  out_ids + r, out_best ? out_best + r : nullptr);
+    }
+  };
+  pool().run(work);
   for (int c : codes)
     if (c != 0) return c;
   return 0;
