@@ -254,23 +254,32 @@ MF_API mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void* out
  * mf_decode_keys" (the reference's single-GPU linear_f16 + greedy_select_f16,
  * src/cuda/linear.cu:40-104 and src/cuda/greedy.cu:237-279, split by vocab
  * rows) with one launch per rank: the kernel's last CTA stores its keys into
- * every rank's exchange buffer over NVLink, waits (bounded, 100 ms) for every
- * rank's keys, and writes the global ids/scores (and merged keys) on every
- * rank.  One process per GPU, one exchange buffer per rank:
+ * every rank's exchange buffer over NVLink, raises the rank's flag there,
+ * waits (bounded, 100 ms) for every rank's flag for this call, and writes
+ * the global ids/scores (and merged keys) on every rank.  One process per GPU, one exchange buffer per
+ * rank:
  *   mf_exchange_alloc      cudaMalloc + zero + cudaIpcGetMemHandle (64-byte handle)
  *   (the caller all-gathers the handles, e.g. over torch.distributed)
  *   mf_exchange_open_peer  cudaIpcOpenMemHandle of a peer's handle
  * exchange[q] is rank q's buffer as mapped in this process (the own buffer
  * at exchange[rank]); world <= 8; every rank calls with the same rows, in
- * the same order, on its own GPU.  A rank whose peers do not arrive within
- * 100 ms gives every row the sentinel; the context stays usable.
- * launch_flags as for mf_dense_head_f16_ex. */
+ * the same order, on its own GPU.
+ * Failure signal: the call returns MF_OK once launched; a rank whose peers
+ * do not arrive within 100 ms, or whose peer reports a failed part, gives
+ * every row MF_INVALID_TOKEN (sentinel rows are the device-side failure
+ * signal) and marks its exchange buffer broken; every later call on a
+ * broken buffer gives the sentinel as well (mf_exchange_broken reads the
+ * mark) until the caller makes new exchange buffers.  The context stays
+ * usable.  launch_flags as for mf_dense_head_f16_ex. */
 #define MF_IPC_HANDLE_BYTES 64
 MF_API uint64_t mf_exchange_bytes(uint64_t rows, uint32_t world);
 MF_API mf_status mf_exchange_alloc(void** buffer, uint64_t bytes, void* ipc_handle);
 MF_API mf_status mf_exchange_free(void* buffer);
 MF_API mf_status mf_exchange_open_peer(const void* ipc_handle, void** peer_buffer);
 MF_API mf_status mf_exchange_close_peer(void* peer_buffer);
+/* 1 in *broken once this rank's exchange buffer (its own, as allocated) is
+ * marked broken, else 0.  Synchronous 4-byte read. */
+MF_API mf_status mf_exchange_broken(const void* buffer, uint32_t* broken);
 MF_API mf_status mf_dense_head_sharded_f16(
     const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
     void* out_keys, uint64_t out_keys_bytes, void* out_ids, uint64_t out_ids_bytes,

@@ -53,6 +53,7 @@ _SIGNATURES["mf_exchange_alloc"] = [ctypes.POINTER(_P), _U64, _P]
 _SIGNATURES["mf_exchange_free"] = [_P]
 _SIGNATURES["mf_exchange_open_peer"] = [_P, ctypes.POINTER(_P)]
 _SIGNATURES["mf_exchange_close_peer"] = [_P]
+_SIGNATURES["mf_exchange_broken"] = [_P, _P]
 _SIGNATURES["mf_dense_head_sharded_f16"] = ([_P, _U64] * 6 + [_U64] * 4
                                             + [_P, _U64, ctypes.c_uint32, ctypes.c_uint32,
                                                ctypes.c_uint32, _P])

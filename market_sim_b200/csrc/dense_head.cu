@@ -41,9 +41,23 @@
 // release, waits (bounded) for every rank's flag in its own buffer, and
 // decodes the maximum.  This replaces a NCCL max all-reduce of the keys and
 // the decode launch.  Exchange buffer of one rank (mf_exchange_bytes):
-//   u32 epoch (this rank's call counter) at 0, u32 flags[world] at 64,
+//   u32 epoch (this rank's call counter) at 0, u32 broken at 4,
+//   u32 flags[world] at 64 (2 x epoch + failed, of rank q's call),
 //   u64 slots[2][world][rows] at 512, parity = epoch & 1, so a rank one call
-//   ahead never overwrites keys a slower rank is still reading.
+//   ahead never overwrites keys a slower rank is still reading (a rank cannot
+//   get two calls ahead: finishing a call needs every rank's flag for it).
+// A flag passes only when it names exactly this call.  A wait that runs out
+// (100 ms) or a peer reporting a failed part gives every row the sentinel
+// and marks the buffer broken: a peer that arrives late could otherwise
+// leave keys of an old call where a later call of the same parity reads, so
+// every later call on a broken buffer gives the sentinel too, until the
+// caller makes new exchange buffers.
+//
+// (Measured and rejected: every CTA max-reducing its rows' keys into every
+// rank's slot as it finishes, 54 us per step on 2 GPUs, and the last CTA of
+// each hidden tile pushing the tile's rows, 44 us, against 38 us for this
+// single push by the last CTA: the merge sits at the end of the kernel
+// either way, and the extra system-scope fences cost more than they hide.)
 //
 // Every mbarrier wait is bounded; a wait that runs out sets an abort flag
 // and the error word in the workspace, and the CTA drains its in-flight
@@ -457,10 +471,12 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       unsigned char* self = p.xbuf[p.rank];
       if (threadIdx.x == 0) {
         s_epoch = *reinterpret_cast<volatile uint32_t*>(self) + 1u;
-        s_xfail = 0u;
+        s_xfail = (failed || *reinterpret_cast<volatile uint32_t*>(self + 4) != 0u) ? 1u : 0u;
       }
       __syncthreads();
       const uint32_t epoch = s_epoch;
+      const uint32_t want = epoch & 0x7FFFFFFFu;
+      const bool own_fail = s_xfail != 0u;
       const size_t par_off = kXSlots + (size_t)(epoch & 1u) * p.world * p.rows * 8;
       for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
         const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
@@ -470,18 +486,23 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       }
       __threadfence_system();
       __syncthreads();
-      if (threadIdx.x < p.world) {
+      if (threadIdx.x < p.world) {  // this rank's flag for this call, in every buffer
         uint32_t* flag = reinterpret_cast<uint32_t*>(p.xbuf[threadIdx.x] + kXFlags) + p.rank;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+        const uint32_t v = (want << 1) | (own_fail ? 1u : 0u);
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
       }
-      if (threadIdx.x < p.world) {
-        // wait (bounded) until rank threadIdx.x has stored this call's keys here
+      if (threadIdx.x < p.world && threadIdx.x != p.rank) {
+        // wait (bounded) until rank threadIdx.x has stored this call's keys
+        // here: the flag must name exactly this call
         const uint32_t* flag = reinterpret_cast<const uint32_t*>(self + kXFlags) + threadIdx.x;
         const uint64_t start = global_ns();
         for (uint32_t i = 0;; ++i) {
           uint32_t v;
           asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-          if ((int32_t)(v - epoch) >= 0) break;
+          if ((v >> 1) == want) {
+            if (v & 1u) atomicOr(&s_xfail, 1u);  // that rank failed its part
+            break;
+          }
           if ((i & 63u) == 63u && global_ns() - start > kWaitLimitNs) {
             atomicOr(&s_xfail, 1u);
             break;
@@ -489,7 +510,7 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
         }
       }
       __syncthreads();
-      const bool xfail = failed || s_xfail != 0u;
+      const bool xfail = s_xfail != 0u;
       if (threadIdx.x == 0 && p.error_out) *p.error_out = xfail ? 1u : 0u;
       const unsigned long long* slots =
           reinterpret_cast<const unsigned long long*>(self + par_off);
@@ -509,7 +530,10 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
         if (p.out_scores)
           p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
       }
-      if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(self) = epoch;
+      if (threadIdx.x == 0) {
+        if (xfail) *reinterpret_cast<volatile uint32_t*>(self + 4) = 1u;  // broken from now on
+        *reinterpret_cast<volatile uint32_t*>(self) = epoch;
+      }
     } else {
       if (threadIdx.x == 0 && p.error_out) *p.error_out = failed ? 1u : 0u;
       for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
@@ -761,6 +785,13 @@ extern "C" mf_status mf_exchange_open_peer(const void* ipc_handle, void** peer_b
   cudaIpcMemHandle_t h;
   memcpy(&h, ipc_handle, sizeof(h));
   const cudaError_t e = cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
+}
+
+extern "C" mf_status mf_exchange_broken(const void* buffer, uint32_t* broken) {
+  if (buffer == nullptr || broken == nullptr) return d_fail(MF_INVALID_ARGUMENT);
+  const cudaError_t e = cudaMemcpy(broken, static_cast<const char*>(buffer) + 4, 4,
+                                   cudaMemcpyDeviceToHost);
   return e == cudaSuccess ? d_ok() : d_fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
 }
 

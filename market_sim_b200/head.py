@@ -364,6 +364,19 @@ def exchange_bytes(rows: int, world: int) -> int:
     return int(lib.mf_exchange_bytes(rows, world))
 
 
+def exchange_broken(buffer) -> int:
+    """1 once a sharded call on this rank's exchange buffer (a device tensor
+    or address) gave up on a peer or saw a peer fail, else 0.  A broken
+    buffer gives every row the sentinel until new buffers are made.  Reads
+    the word synchronously."""
+    ptr = buffer.data_ptr() if hasattr(buffer, "data_ptr") else int(buffer)
+    out = ctypes.c_uint32()
+    st = _status(lib.mf_exchange_broken(ctypes.c_void_p(ptr), ctypes.byref(out)))
+    if not st.ok():
+        raise RuntimeError(f"mf_exchange_broken failed: {st}")
+    return int(out.value)
+
+
 def dense_head_sharded_f16(hidden: Buffer, embedding: Buffer, keys: Optional[Buffer],
                            token_ids: Optional[Buffer], scores: Optional[Buffer],
                            workspace: Buffer, rows: int, hidden_size: int, vocab_rows: int,

@@ -178,9 +178,14 @@ def _slot(buf, rows, world, epoch, q):
 
 
 def _flag(buf, q):
+    """Rank q's flag in one exchange buffer: 2 x epoch + failed."""
     import torch
 
     return buf[64 + 4 * q:64 + 4 * q + 4].view(torch.int32)
+
+
+def _broken(buf):
+    return int(buf[4:8].view(__import__("torch").int32).item())
 
 
 def test_dense_sharded_merge_emulated_peer(mf):
@@ -188,7 +193,8 @@ def test_dense_sharded_merge_emulated_peer(mf):
     are stored into rank 0's exchange buffer beforehand (as rank 1 would over
     NVLink), so rank 0's kernel never waits on another launch.  Over three
     calls (epochs 1-3, both slot parities) rank 0's ids / scores / keys equal
-    the unsharded head, and rank 0's keys and flag land in the peer buffer."""
+    the unsharded head, and rank 0's keys and flag (2 x epoch) land in the
+    peer buffer."""
     import torch
 
     from market_sim_b200 import synth
@@ -209,7 +215,7 @@ def test_dense_sharded_merge_emulated_peer(mf):
     ws = torch.zeros(mf.dense_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
     for epoch in (1, 2, 3):
         _slot(own, rows, world, epoch, 1).copy_(torch.from_numpy(k1.view(np.int64)))
-        _flag(own, 1).fill_(epoch)
+        _flag(own, 1).fill_(2 * epoch)
         keys = torch.empty(rows, dtype=torch.int64, device="cuda")
         ids = torch.empty(rows, dtype=torch.int32, device="cuda")
         sc = torch.empty(rows, dtype=torch.float32, device="cuda")
@@ -221,8 +227,9 @@ def test_dense_sharded_merge_emulated_peer(mf):
         assert np.array_equal(ids.cpu().numpy().view(np.uint32), full_ids)
         assert np.array_equal(sc.cpu().numpy().view(np.uint32), full_sc.view(np.uint32))
         assert np.array_equal(_slot(peer, rows, world, epoch, 0).cpu().numpy().view(np.uint64), k0)
-        assert int(_flag(peer, 0).item()) == epoch
+        assert int(_flag(peer, 0).item()) == 2 * epoch
         assert int(own[:4].view(torch.int32).item()) == epoch
+        assert _broken(own) == 0
         assert int(ws.sum()) == 0
 
 
@@ -248,8 +255,45 @@ def test_dense_sharded_peer_never_arrives(mf):
     torch.cuda.synchronize()
     assert (ids.cpu().numpy().view(np.uint32) == INVALID).all()
     assert int(ws.sum()) == 0
+    assert _broken(own) == 1 and mf.exchange_broken(own) == 1
     _, ids2, _ = _dense(mf, h_d, e_d, rows, hs, vocab)
     assert (ids2 < vocab).all()
+
+
+def test_dense_sharded_stale_or_failed_peer_gives_sentinel(mf):
+    """Exact epoch match: a peer flag naming another call (two calls ahead)
+    never passes, so the wait runs out and every row gets the sentinel
+    instead of decoding keys of another call; a peer flag with the failed
+    bit set gives the sentinel at once.  Either way the buffer is marked
+    broken and later calls on it give the sentinel too."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    rows, vocab, hs, world = 128, 1024, 576, 2
+    e_d = to_dev(synth.embedding(97, vocab=vocab))
+    h_d = to_dev(synth.hidden_states(98, rows))
+    nbytes = mf.exchange_bytes(rows, world)
+    ws = torch.zeros(mf.dense_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    for flag in (2 * 3, 2 * 1 + 1):  # epoch 3 while this call is epoch 1; epoch 1 failed
+        own = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        peer = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        ex = _Exchange([own.data_ptr(), peer.data_ptr()], nbytes, world, 0)
+        _flag(own, 1).fill_(flag)
+        ids = torch.zeros(rows, dtype=torch.int32, device="cuda")
+        st = mf.dense_head_sharded_f16(h_d, e_d, None, ids, None, ws, rows, hs, vocab, 0, ex,
+                                       gpu_stream())
+        assert st.ok(), st
+        torch.cuda.synchronize()
+        assert (ids.cpu().numpy().view(np.uint32) == INVALID).all()
+        assert _broken(own) == 1
+        _flag(own, 1).fill_(2 * 2)  # even a matching flag for the next call: still broken
+        st = mf.dense_head_sharded_f16(h_d, e_d, None, ids, None, ws, rows, hs, vocab, 0, ex,
+                                       gpu_stream())
+        assert st.ok(), st
+        torch.cuda.synchronize()
+        assert (ids.cpu().numpy().view(np.uint32) == INVALID).all()
+        assert int(ws.sum()) == 0
 
 
 def test_dense_sharded_rejects(mf):

@@ -420,6 +420,31 @@ def test_host_pipeline_packed_batches(mf, emb_full):
     pipe.close()
 
 
+def test_host_pipeline_wait_on_reused_slot(mf, emb_full):
+    """More batches than slots, then wait(ticket 0) alone: the first batch's
+    slot has been reused since, and wait must still not return before that
+    batch's results are home (its slot's stream holds them in order)."""
+    import torch
+
+    e, e_dev = emb_full
+    depth = 2
+    pipe = mf.HostPipeline(e_dev, 256, 600_000, depth=depth)
+    cases = [_ragged_case(900 + i, 256, 4096) for i in range(2 * depth + 1)]
+    outs, tickets = [], []
+    for h, off, ids in cases:
+        b = mf.HostPipeline.pack(h, off, ids)
+        o = torch.full((2 * len(h),), -7, dtype=torch.int32).pin_memory()
+        tickets.append(pipe.submit_packed(b, len(h), ids.size, o))
+        outs.append((b, o))
+    pipe.wait(tickets[0])
+    h, off, ids = cases[0]
+    got = outs[0][1].numpy()[:256].view(np.uint32).copy()
+    pipe.synchronize()
+    want, _, _ = _csr_call(mf, h, e_dev, off, ids)
+    assert np.array_equal(got, want)
+    pipe.close()
+
+
 @pytest.mark.parametrize("rows,kmax,hs", [(64, 4096, 576), (9, 40, 64)])
 def test_fused_rmsnorm_head_vs_oracle(mf, O, rows, kmax, hs):
     """Final RMSNorm fused into the head: equals the oracle's rms_norm_f32
