@@ -163,7 +163,9 @@ def run_ours(args):
               "decode": lambda: bench_decode(emb, replicas[0], device, rank, stream, identity),
               "ksweep": lambda: bench_k_sweep(replicas, device, stream),
               "rmsnorm": lambda: bench_rmsnorm_fused(batches, replicas, device, stream),
-              "market": lambda: bench_market_decode(emb, replicas[0], device, stream)}[args.only]
+              "market": lambda: bench_market_decode(emb, replicas[0], device, stream),
+              "refgpu": lambda: bench_reference_gpu(emb, replicas[0], batches, device,
+                                                    stream)}[args.only]
         res = fn()
         if rank == 0:
             print(json.dumps({"only": args.only, **res}), flush=True)
@@ -373,6 +375,7 @@ def run_ours(args):
                                               rows_per_launch=10_000, states=1, launches=4),
             "rmsnorm_fused_head": bench_rmsnorm_fused(batches, replicas, device, stream),
             "market_dfa_decode": bench_market_decode(emb, replicas[0], device, stream),
+            "reference_gpu": bench_reference_gpu(emb, replicas[0], batches, device, stream),
         }
     if rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(batches[0], emb, budget_s=args.cpu_seconds)
@@ -688,6 +691,108 @@ def bench_k_sweep(replicas, device, stream, rows_per_launch=1, states=16, launch
     return {"workload": f"{rows_per_launch} hidden state(s) per launch, K ids uniform without "
                         f"replacement, {states} state set(s) x {len(replicas)} embedding copies",
             "results": out}
+
+
+REF_CELLS = [(r, k) for r in (1, 16, 256) for k in (2, 8, 32, 128)]
+
+
+def bench_reference_gpu(emb, e_dev, batches, device, stream, launches=200):
+    """Same-GPU comparator: the reference's own CUDA restricted head
+    (restricted_output_head_f16, src/cuda/greedy.cu:133-212 via its wrapper
+    :349-414; oracle/_ref/libmfref_gpu.so, built from the reference's
+    sources for sm_100a) against this repository's kernel with the same
+    reference signature (mf_restricted_output_head_f16, padded table), on
+    the reference bench's 12 cells (rows x allowed, patterned hidden rows
+    and ids, src/tools/cuda_restricted_output_head_bench.cu:129-140,278-291)
+    and on the headline batch padded to 4,096 ids per row, beside the ragged
+    CSR head on that batch.  Each: `launches` back-to-back launches in one
+    CUDA graph on the launching stream, events around a replay; ids
+    compared."""
+    import torch
+
+    from market_sim_b200 import head
+    from oracle import oracle as O
+
+    if not O.ref_gpu_available():
+        return {"unavailable": "oracle/_ref/libmfref_gpu.so was not built (needs the reference "
+                               "sources at build time)"}
+    v = emb.shape[0]
+
+    def timed(launch, s_handle, n):
+        """Device time per launch: n launches captured in one CUDA graph on
+        the launching stream, events around a replay."""
+        st_ = torch.cuda.ExternalStream(s_handle, device=device)
+        for _ in range(3):
+            launch()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st_):
+            for _ in range(n):
+                launch()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st_):
+            a.record(st_)
+            g.replay()
+            b.record(st_)
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) * 1e3 / n
+
+    def one(h, allowed, counts, k):
+        rows = h.shape[0]
+        h_d, a_d, c_d = (torch.from_numpy(x).to(device) for x in (h, allowed, counts))
+        ref = O.RefGpuHead(h_d, e_dev, a_d, c_d, k)
+        try:
+            out = torch.empty(rows, dtype=torch.int32, device=device)
+            hs = stream.cuda_stream
+
+            def ours():
+                st = head.restricted_output_head_f16(h_d, e_dev, a_d, c_d, out, rows, 576, v, k,
+                                                     hs)
+                if not st.ok():
+                    raise RuntimeError(f"padded head failed: {st}")
+
+            n = launches if rows * k < 100_000 else max(20, launches // 10)
+            ref_us = timed(ref.run, ref.stream(), n)
+            our_us = timed(ours, hs, n)
+            same = int((ref.ids() == out.cpu().numpy().view(np.uint32)).sum())
+        finally:
+            ref.close()
+        return {"reference_us": round(ref_us, 3), "ours_us": round(our_us, 3),
+                "vs_reference_gpu": round(ref_us / our_us, 2), "ids_equal": same, "rows": rows}
+
+    cells = {}
+    for rows, k in REF_CELLS:
+        h = np.array([0.5 + (i % 13) / 32.0 for i in range(rows * 576)],
+                     np.float32).astype(np.float16).reshape(rows, 576)
+        allowed = np.array([[(r * 131 + c * 977 + 17) % v for c in range(k)]
+                            for r in range(rows)], np.uint32)
+        cells[f"rows={rows},k={k}"] = one(h, allowed, np.full(rows, k, np.uint32), k)
+    b = batches[0]
+    counts = np.diff(b["off"]).astype(np.uint32)
+    kmax = KMAX
+    allowed = np.zeros((ROWS, kmax), np.uint32)
+    for r in range(ROWS):
+        allowed[r, :counts[r]] = b["ids"][b["off"][r]:b["off"][r + 1]]
+    headline = one(b["hid"], allowed, counts, kmax)
+    ws = torch.zeros(head.head_workspace_bytes(ROWS), dtype=torch.uint8, device=device)
+    o_ids = torch.empty(ROWS, dtype=torch.int32, device=device)
+
+    def ragged():
+        st = head.restricted_output_head_csr_f16(b["hid_d"], e_dev, b["off_d"], b["ids_d"], o_ids,
+                                                 None, ws, ROWS, 576, v, stream.cuda_stream)
+        if not st.ok():
+            raise RuntimeError(f"head failed: {st}")
+
+    headline["ours_ragged_csr_us"] = round(timed(ragged, stream.cuda_stream, launches), 3)
+    headline["vs_reference_gpu_ragged"] = round(headline["reference_us"] /
+                                                headline["ours_ragged_csr_us"], 2)
+    return {"workload": "reference restricted_output_head_f16 (its own CUDA source, sm_100a) vs "
+                        "this repository's kernels on the same B200; 12 reference bench cells "
+                        "and the headline batch padded to 4096 ids per row",
+            "cells": cells, "headline_padded_4096": headline}
 
 
 def _tensor_peak():
@@ -1029,7 +1134,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["dense", "decode", "ksweep", "rmsnorm", "market"],
+    ap.add_argument("--only", choices=["dense", "decode", "ksweep", "rmsnorm", "market", "refgpu"],
                     help="run one secondary workload alone and print its result (profiling)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the dense full-vocab and DFA-decode measurements")

@@ -17,6 +17,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libmfref.so")
+REF_GPU_LIB = os.path.join(HERE, "_ref", "libmfref_gpu.so")
 INVALID = 0xFFFFFFFF
 
 _P = ctypes.c_void_p
@@ -280,6 +281,69 @@ def ref_head_csr_by_sequence(hidden_f16, emb_f32, offsets, ids, threads=1):
         _p(out), _p(best), threads)
     assert code == 0, code
     return out, best
+
+
+def ref_gpu_available() -> bool:
+    return os.path.exists(REF_GPU_LIB)
+
+
+class RefGpuHead:
+    """The reference's own CUDA restricted head (oracle/_ref/libmfref_gpu.so:
+    marketforge::cuda::restricted_output_head_f16 from src/cuda/greedy.cu,
+    through its DeviceBuffer / CudaStream types) on one padded problem.
+    Inputs are copied into the reference's own buffers from device tensors;
+    run() launches on the reference's stream (stream() gives its handle)."""
+
+    _lib = None
+
+    @classmethod
+    def lib(cls):
+        if cls._lib is None:
+            r = ctypes.CDLL(REF_GPU_LIB)
+            r.mfrefgpu_create.argtypes = [_U64, _U64, _U64, _U64]
+            r.mfrefgpu_create.restype = _P
+            r.mfrefgpu_upload.argtypes = [_P, ctypes.c_int, _P, _U64]
+            r.mfrefgpu_run.argtypes = [_P]
+            r.mfrefgpu_stream.argtypes = [_P]
+            r.mfrefgpu_stream.restype = _P
+            r.mfrefgpu_download.argtypes = [_P, _P]
+            r.mfrefgpu_destroy.argtypes = [_P]
+            cls._lib = r
+        return cls._lib
+
+    def __init__(self, hidden, embedding, allowed, counts, max_allowed):
+        """Device tensors: hidden fp16 [rows, H], embedding fp16 [V, H],
+        allowed u32/i32 [rows, max_allowed], counts u32/i32 [rows]."""
+        rows, h = int(hidden.shape[0]), int(hidden.shape[1])
+        self.rows = rows
+        self.ctx = self.lib().mfrefgpu_create(rows, h, int(embedding.shape[0]), int(max_allowed))
+        if not self.ctx:
+            raise RuntimeError("reference CUDA context allocation failed")
+        for which, t in enumerate((hidden, embedding, allowed, counts)):
+            code = self.lib().mfrefgpu_upload(self.ctx, which, t.data_ptr(),
+                                              t.numel() * t.element_size())
+            if code:
+                raise RuntimeError(f"reference upload {which} failed: {code}")
+
+    def run(self) -> None:
+        code = self.lib().mfrefgpu_run(self.ctx)
+        if code:
+            raise RuntimeError(f"reference restricted_output_head_f16 failed: {code}")
+
+    def stream(self) -> int:
+        return int(self.lib().mfrefgpu_stream(self.ctx) or 0)
+
+    def ids(self) -> np.ndarray:
+        out = np.empty(self.rows, np.uint32)
+        code = self.lib().mfrefgpu_download(self.ctx, _p(out))
+        if code:
+            raise RuntimeError(f"reference download failed: {code}")
+        return out
+
+    def close(self) -> None:
+        if self.ctx:
+            self.lib().mfrefgpu_destroy(self.ctx)
+            self.ctx = None
 
 
 def ref_market_dfa():
