@@ -184,6 +184,21 @@ MF_API mf_status mf_dfa_head_step_f16(const void* hidden, uint64_t hidden_bytes,
                                uint64_t batch, uint64_t num_states, uint64_t hidden_size,
                                uint64_t vocab, void* stream);
 
+/* mf_dfa_head_step_f16 with the decoder's final RMSNorm fused in front, as
+ * mf_head_restricted_csr_rmsnorm_f16: hidden holds the last layer's
+ * un-normalised rows, gamma the norm weight (fp16 [hidden_size], 16-byte
+ * aligned), eps finite and > 0.  One launch for rms_norm_f16 + the grammar's
+ * allowed-set lookup + the head + the DFA advance. */
+MF_API mf_status mf_dfa_head_step_rmsnorm_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* gamma, uint64_t gamma_bytes, float eps,
+    const void* embedding, uint64_t embedding_bytes, const void* state_offsets,
+    uint64_t state_offsets_bytes, const void* arc_tokens, uint64_t arc_tokens_bytes,
+    const void* arc_next, uint64_t arc_next_bytes, const void* states_in,
+    uint64_t states_in_bytes, void* states_out, uint64_t states_out_bytes, void* out_tokens,
+    uint64_t out_tokens_bytes, void* out_scores, uint64_t out_scores_bytes, void* workspace,
+    uint64_t workspace_bytes, uint64_t batch, uint64_t num_states, uint64_t hidden_size,
+    uint64_t vocab, void* stream);
+
 /* `steps` DFA head steps back to back on one stream with no host
  * synchronisation: hidden is fp16 [steps, batch, hidden_size];
  * state_trace is u32 [steps + 1, batch] with row 0 holding the initial

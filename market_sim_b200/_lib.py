@@ -44,6 +44,8 @@ _SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U6
 _SIGNATURES["mf_head_restricted_csr_rmsnorm_f16"] = [_P, _U64, _P, _U64, ctypes.c_float, _P, _U64,
                                                      _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
                                                      _U64, _U64, _U64, _U64, _P]
+_SIGNATURES["mf_dfa_head_step_rmsnorm_f16"] = ([_P, _U64] * 2 + [ctypes.c_float] + [_P, _U64] * 9
+                                               + [_U64] * 4 + [_P])
 _SIGNATURES["mf_dense_head_f16"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64, _P, _U64,
                                     _U64, _U64, _U64, _U64, _P]
 _SIGNATURES["mf_dense_selftest_wait_timeout"] = [_P, ctypes.POINTER(ctypes.c_uint32),

@@ -850,10 +850,10 @@ static DeviceInfo& device_info() {
         if (b < 1) b = 1;
     // DFA mode keeps 2 x batch + 1 ints in shared memory (up to ~64 KB)
     const int dfa_smem = (2 * kMaxDfaBatch + 1) * (int)sizeof(int32_t);
-    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kDfa, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, dfa_smem);
-    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kDfa, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, dfa_smem);
+    for (auto k : {ragged_head_kernel<RowMode::kDfa, false>, ragged_head_kernel<RowMode::kDfa, true>,
+                   ragged_head_kernel<RowMode::kDfa, false, true>,
+                   ragged_head_kernel<RowMode::kDfa, true, true>})
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dfa_smem);
   }
   return d;
 }
@@ -1081,23 +1081,27 @@ cudaError_t dfa_launch(RaggedParams p, bool fast, cudaStream_t s, bool after_ste
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  cudaError_t e = fast ? cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, true>, p,
-                                            (int64_t)0)
-                       : cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, false>, p,
-                                            (int64_t)0);
+  cudaError_t e;
+  if (p.gamma != nullptr)
+    e = fast ? cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, true, true>, p, (int64_t)0)
+             : cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, false, true>, p,
+                                  (int64_t)0);
+  else
+    e = fast ? cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, true>, p, (int64_t)0)
+             : cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kDfa, false>, p, (int64_t)0);
   return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 }  // namespace
 
-extern "C" mf_status mf_dfa_head_step_f16(
+static mf_status dfa_step(
     const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
     const void* state_offsets, uint64_t state_offsets_bytes, const void* arc_tokens,
     uint64_t arc_tokens_bytes, const void* arc_next, uint64_t arc_next_bytes,
     const void* states_in, uint64_t states_in_bytes, void* states_out, uint64_t states_out_bytes,
     void* out_tokens, uint64_t out_tokens_bytes, void* out_scores, uint64_t out_scores_bytes,
     void* workspace, uint64_t workspace_bytes, uint64_t batch, uint64_t num_states,
-    uint64_t hidden_size, uint64_t vocab, void* stream) {
+    uint64_t hidden_size, uint64_t vocab, void* stream, const void* gamma, float eps) {
   mf_status st = dfa_validate(hidden, hidden_bytes, embedding, embedding_bytes, state_offsets,
                               state_offsets_bytes, arc_tokens, arc_tokens_bytes, arc_next,
                               arc_next_bytes, 1, batch, num_states, hidden_size, vocab, stream);
@@ -1123,9 +1127,48 @@ extern "C" mf_status mf_dfa_head_step_f16(
   p.rows = (uint32_t)batch;
   p.hidden_size = (uint32_t)hidden_size;
   p.vocab = (uint32_t)vocab;
+  p.gamma = static_cast<const __half*>(gamma);
+  p.eps = eps;
   split_workspace(workspace, batch, p);
   return launch_status(dfa_launch(p, fast_path(hidden, embedding, hidden_size),
                                   static_cast<cudaStream_t>(stream), false));
+}
+
+extern "C" mf_status mf_dfa_head_step_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* state_offsets, uint64_t state_offsets_bytes, const void* arc_tokens,
+    uint64_t arc_tokens_bytes, const void* arc_next, uint64_t arc_next_bytes,
+    const void* states_in, uint64_t states_in_bytes, void* states_out, uint64_t states_out_bytes,
+    void* out_tokens, uint64_t out_tokens_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t batch, uint64_t num_states,
+    uint64_t hidden_size, uint64_t vocab, void* stream) {
+  return dfa_step(hidden, hidden_bytes, embedding, embedding_bytes, state_offsets,
+                  state_offsets_bytes, arc_tokens, arc_tokens_bytes, arc_next, arc_next_bytes,
+                  states_in, states_in_bytes, states_out, states_out_bytes, out_tokens,
+                  out_tokens_bytes, out_scores, out_scores_bytes, workspace, workspace_bytes, batch,
+                  num_states, hidden_size, vocab, stream, nullptr, 0.f);
+}
+
+extern "C" mf_status mf_dfa_head_step_rmsnorm_f16(
+    const void* hidden, uint64_t hidden_bytes, const void* gamma, uint64_t gamma_bytes, float eps,
+    const void* embedding, uint64_t embedding_bytes, const void* state_offsets,
+    uint64_t state_offsets_bytes, const void* arc_tokens, uint64_t arc_tokens_bytes,
+    const void* arc_next, uint64_t arc_next_bytes, const void* states_in,
+    uint64_t states_in_bytes, void* states_out, uint64_t states_out_bytes, void* out_tokens,
+    uint64_t out_tokens_bytes, void* out_scores, uint64_t out_scores_bytes, void* workspace,
+    uint64_t workspace_bytes, uint64_t batch, uint64_t num_states, uint64_t hidden_size,
+    uint64_t vocab, void* stream) {
+  // rms_norm_f32's own checks (src/cpu/operators.cpp:498-501): finite eps > 0
+  if (!(eps > 0.f) || !(eps < 3.0e38f) || gamma == nullptr) return fail(MF_INVALID_ARGUMENT);
+  if (gamma_bytes != hidden_size * 2 || (uintptr_t)gamma % 16 != 0) return fail(MF_INVALID_ARGUMENT);
+  if (gamma == hidden || gamma == embedding || gamma == states_out || gamma == out_tokens ||
+      gamma == out_scores || gamma == workspace)
+    return fail(MF_INVALID_ARGUMENT);
+  return dfa_step(hidden, hidden_bytes, embedding, embedding_bytes, state_offsets,
+                  state_offsets_bytes, arc_tokens, arc_tokens_bytes, arc_next, arc_next_bytes,
+                  states_in, states_in_bytes, states_out, states_out_bytes, out_tokens,
+                  out_tokens_bytes, out_scores, out_scores_bytes, workspace, workspace_bytes, batch,
+                  num_states, hidden_size, vocab, stream, gamma, eps);
 }
 
 extern "C" mf_status mf_dfa_decode_f16(

@@ -311,6 +311,21 @@ def dfa_head_step_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer,
         batch, num_states, hidden_size, vocabulary_size, _sp(stream)))
 
 
+def dfa_head_step_rmsnorm_f16(hidden: Buffer, gamma: Buffer, eps: float, embedding: Buffer,
+                              state_offsets: Buffer, arc_tokens: Buffer, arc_next: Buffer,
+                              states_in: Buffer, states_out: Buffer, tokens: Buffer,
+                              scores: Optional[Buffer], workspace: Buffer, batch: int,
+                              num_states: int, hidden_size: int, vocabulary_size: int,
+                              stream) -> Status:
+    """One device step with the final RMSNorm fused in front (hidden = the
+    last layer's un-normalised rows, gamma = the norm weight)."""
+    return _status(lib.mf_dfa_head_step_rmsnorm_f16(
+        *_pb(hidden), *_pb(gamma), float(eps), *_pb(embedding), *_pb(state_offsets),
+        *_pb(arc_tokens), *_pb(arc_next), *_pb(states_in), *_pb(states_out), *_pb(tokens),
+        *_pb(scores), *_pb(workspace), batch, num_states, hidden_size, vocabulary_size,
+        _sp(stream)))
+
+
 def dfa_decode_f16(hidden: Buffer, embedding: Buffer, state_offsets: Buffer, arc_tokens: Buffer,
                    arc_next: Buffer, state_trace: Buffer, token_trace: Buffer,
                    score_trace: Optional[Buffer], workspace: Buffer, steps: int, batch: int,
