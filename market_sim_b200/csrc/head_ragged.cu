@@ -390,7 +390,8 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
                                                int64_t c_begin, int64_t c_end, int sub,
                                                unsigned gmask, uint4* slot,
                                                const BlockSlots& bs, BlockRowTable& tab,
-                                               uint32_t* s_rows_found) {
+                                               uint32_t* s_rows_found, bool rows_known,
+                                               uint32_t known_first, uint32_t known_last) {
   const uint4* emb = reinterpret_cast<const uint4*>(p.embedding);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int64_t c = c_begin;
@@ -417,14 +418,18 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
   if (c < c_end) issue();
 
   // ---- the block's rows: [first, last] covering [bs.begin, bs.end) ----
-  if (warp == 0 && lane < 16) {  // group 0: first row, group 1: last row
-    const int64_t at = lane < 8 ? bs.begin : bs.end - 1;
-    uint32_t r = 0;
-    if (bs.begin < bs.end) r = find_row<RowMode::kCsr>(rows_tab, p.rows, at, sub, gmask);
-    if (sub == 0) s_rows_found[lane >> 3] = r;
+  // (small batches: counted by the kernel's offset check on entry)
+  if (!rows_known) {
+    if (warp == 0 && lane < 16) {  // group 0: first row, group 1: last row
+      const int64_t at = lane < 8 ? bs.begin : bs.end - 1;
+      uint32_t r = 0;
+      if (bs.begin < bs.end) r = find_row<RowMode::kCsr>(rows_tab, p.rows, at, sub, gmask);
+      if (sub == 0) s_rows_found[lane >> 3] = r;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  const uint32_t first = s_rows_found[0], last = s_rows_found[1];
+  const uint32_t first = rows_known ? known_first : s_rows_found[0];
+  const uint32_t last = rows_known ? known_last : s_rows_found[1];
   const int64_t span = (int64_t)last - (int64_t)first + 1;
   tab.first = first;
   tab.n = (bs.begin < bs.end && span >= 1 && span <= kBlockRows) ? (int)span : 0;
@@ -564,6 +569,9 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
 
   Rows<M> rows_tab;
   int64_t total;
+  __shared__ uint32_t s_row_counts[kThreads / 32][2];
+  bool rows_known = false;  // CSR, small batches: the block's first and last rows
+  uint32_t known_first = 0, known_last = 0;
   if (M == RowMode::kCsr) {
     // Overlapped launches: the next batch's blocks may start as this one's
     // retire.  Reads of this call's inputs need no wait (the caller promises
@@ -573,11 +581,30 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     rows_tab.start = p.offsets;
     total = p.total;
     if (p.rows <= kLocalCheckRows) {
+      // One pass over the offsets: the check, and (fast path) how many
+      // rows start at or before the block's first and last candidate,
+      // which gives the rows the block covers without a search.
+      const int64_t b0 = min(p.total, (int64_t)blockIdx.x * kGroupsPerBlock * chunk);
+      const int64_t b1 = min(p.total, b0 + (int64_t)kGroupsPerBlock * chunk) - 1;
       int bad = 0;
-      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads)
-        bad |= __ldg(p.offsets + r) > __ldg(p.offsets + r + 1);
+      uint32_t n0 = 0, n1 = 0;
+      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+        const int32_t o = __ldg(p.offsets + r);
+        bad |= o > __ldg(p.offsets + r + 1);
+        n0 += (int64_t)o <= b0;
+        n1 += (int64_t)o <= b1;
+      }
       if (threadIdx.x == 0)
         bad |= __ldg(p.offsets) != 0 || (int64_t)__ldg(p.offsets + p.rows) != p.total;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        n0 += __shfl_xor_sync(0xFFFFFFFFu, n0, o);
+        n1 += __shfl_xor_sync(0xFFFFFFFFu, n1, o);
+      }
+      if ((threadIdx.x & 31) == 0) {
+        s_row_counts[threadIdx.x >> 5][0] = n0;
+        s_row_counts[threadIdx.x >> 5][1] = n1;
+      }
       if (__syncthreads_or(bad)) {  // malformed: sentinel for this block's rows only
         pdl_wait();
         for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows;
@@ -587,6 +614,15 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
         }
         return;
       }
+      n0 = n1 = 0;
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) {
+        n0 += s_row_counts[w][0];
+        n1 += s_row_counts[w][1];
+      }
+      rows_known = true;
+      known_first = n0 > 0 ? n0 - 1 : 0u;
+      known_last = n1 > 0 ? n1 - 1 : 0u;
     }
   } else {
     pdl_trigger();  // the next decode step's blocks may queue behind this one's
@@ -669,7 +705,8 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     tab.rows = s_hid + kThreads * kFastChunksPerLane;  // after the per-lane slots
     tab.start = s_tab_start;
     csr_fast_block<kNorm>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
-                          c_end, sub, gmask, s_hid + threadIdx.x, bs, tab, s_rows_found);
+                          c_end, sub, gmask, s_hid + threadIdx.x, bs, tab, s_rows_found,
+                          rows_known, known_first, known_last);
   } else if (c_begin < c_end) {
     uint32_t r = find_row<M>(rows_tab, p.rows, c_begin, sub, gmask);
     int64_t row_b = rows_tab.at(r);
