@@ -155,3 +155,30 @@ def test_greedy_rejections(lib):
     assert f(_p(0), 16, _p(1), 4, 1, 7, st).code == E.invalid_argument
     assert f(_p(0), 16, _p(1), 4, 1, 2**32, st).code == E.resource_limit
     assert f(_p(0), 16, _p(0), 4, 1, 8, st).code == E.invalid_argument
+
+
+def test_dfa_rmsnorm_step_rejections(lib):
+    """mf_dfa_head_step_rmsnorm_f16: rms_norm_f32's own checks on eps
+    (src/cpu/operators.cpp:498-501), the norm weight's size, alignment and
+    aliasing, then the plain step's validation."""
+    from market_sim_b200.head import ErrorCode as E
+
+    f = lib.lib.mf_dfa_head_step_rmsnorm_f16
+    batch, ns, hs, v, arcs = 4, 5, 576, 1000, 9
+    ws = lib.lib.mf_dfa_workspace_bytes(batch)
+
+    def call(eps=1e-5, gamma=1, gamma_bytes=hs * 2, batch=batch, stream=STREAM):
+        s = [batch * hs * 2, gamma_bytes, v * hs * 2, (ns + 1) * 4, arcs * 4, arcs * 4,
+             batch * 4, batch * 4, batch * 4, batch * 4, ws]
+        p = [_p(0), _p(gamma), _p(2), _p(3), _p(4), _p(5), _p(6), _p(7), _p(8), _p(9), _p(10)]
+        args = [p[0], s[0], p[1], s[1], ctypes.c_float(eps)]
+        for i in range(2, 11):
+            args += [p[i], s[i]]
+        return f(*args, batch, ns, hs, v, ctypes.c_void_p(stream) if stream else None).code
+
+    assert call(eps=0.0) == E.invalid_argument
+    assert call(eps=float("inf")) == E.invalid_argument
+    assert call(gamma_bytes=hs * 2 - 2) == E.invalid_argument
+    assert call(gamma=0) == E.invalid_argument  # the norm weight aliases the hidden rows
+    assert call(batch=0) == E.invalid_argument
+    assert call(stream=0) == E.invalid_argument
