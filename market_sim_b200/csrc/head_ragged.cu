@@ -45,6 +45,11 @@ struct RaggedParams {
   const uint32_t* states_in;
   uint32_t* states_out;
   uint32_t num_states;
+  // DFA mode with vocab <= 65,536 and num_states < 65,535: a key's id field
+  // packs (token << 16 | next state) instead of the arc's position, so the
+  // row's finaliser needs no table loads (arcs are sorted by token, so the
+  // lowest token is the lowest position: the selection order is the same).
+  uint32_t dfa_packed;
   int64_t num_arcs;
   // outputs
   uint32_t* out_ids;
@@ -123,6 +128,12 @@ __device__ void finalize_row(const RaggedParams& p, const Rows<M>& rows_tab, uin
     p.out_ids[r] = ok ? key_id(key) : kInvalid;
     if (p.out_scores) p.out_scores[r] = ok ? key_score(key) : __uint_as_float(0x7FC00000u);
   } else {
+    if (p.dfa_packed && key_is_result(key)) {
+      p.out_ids[r] = key_id(key) >> 16;
+      p.states_out[r] = key_id(key) & 0xFFFFu;
+      if (p.out_scores) p.out_scores[r] = key_score(key);
+      return;
+    }
     const uint32_t st = p.states_in[r];
     if (key_is_result(key)) {
       const int64_t arc = (int64_t)rows_tab.arc_base[r] + key_id(key);
@@ -756,7 +767,16 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
           t[j] = (uint32_t)p.ids[arc_base + c + j];
         }
         v[j] = j < n_here && t[j] < p.vocab;
-        id[j] = (M == RowMode::kCsr) ? t[j] : (uint32_t)(c + j - row_b);
+        if constexpr (M == RowMode::kCsr) {
+          id[j] = t[j];
+        } else if (p.dfa_packed) {
+          // the next state is read beside the token (same latency); one out
+          // of range becomes 0xFFFF, itself out of range for these tables
+          const uint32_t nx = j < n_here ? p.arc_next[arc_base + c + j] : 0u;
+          id[j] = (t[j] << 16) | (nx < 0xFFFFu ? nx : 0xFFFFu);
+        } else {
+          id[j] = (uint32_t)(c + j - row_b);
+        }
       }
       float sc[R];
       if (kFast) {
@@ -1166,6 +1186,7 @@ static mf_status dfa_step(
   p.vocab = (uint32_t)vocab;
   p.gamma = static_cast<const __half*>(gamma);
   p.eps = eps;
+  p.dfa_packed = vocab <= 65536u && num_states < 65535u ? 1u : 0u;
   split_workspace(workspace, batch, p);
   return launch_status(dfa_launch(p, fast_path(hidden, embedding, hidden_size),
                                   static_cast<cudaStream_t>(stream), false));
@@ -1244,6 +1265,7 @@ extern "C" mf_status mf_dfa_decode_f16(
     p.rows = (uint32_t)batch;
     p.hidden_size = (uint32_t)hidden_size;
     p.vocab = (uint32_t)vocab;
+    p.dfa_packed = vocab <= 65536u && num_states < 65535u ? 1u : 0u;
     split_workspace(workspace, batch, p);
     const cudaError_t e = dfa_launch(p, fast, s, step > 0);
     if (e != cudaSuccess) return launch_status(e);
