@@ -165,7 +165,8 @@ def run_ours(args):
               "rmsnorm": lambda: bench_rmsnorm_fused(batches, replicas, device, stream),
               "market": lambda: bench_market_decode(emb, replicas[0], device, stream),
               "refgpu": lambda: bench_reference_gpu(emb, replicas[0], batches, device,
-                                                    stream)}[args.only]
+                                                    stream),
+              "config1": lambda: bench_config1(emb, replicas[0], device, stream)}[args.only]
         res = fn()
         if rank == 0:
             print(json.dumps({"only": args.only, **res}), flush=True)
@@ -376,6 +377,8 @@ def run_ours(args):
             "rmsnorm_fused_head": bench_rmsnorm_fused(batches, replicas, device, stream),
             "market_dfa_decode": bench_market_decode(emb, replicas[0], device, stream),
             "reference_gpu": bench_reference_gpu(emb, replicas[0], batches, device, stream),
+            "config1_single_sequence": bench_config1(emb, replicas[0], device, stream,
+                                                     cpu=not args.no_cpu),
         }
     if rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(batches[0], emb, budget_s=args.cpu_seconds)
@@ -690,6 +693,94 @@ def bench_k_sweep(replicas, device, stream, rows_per_launch=1, states=16, launch
     return {"workload": f"{rows_per_launch} hidden state(s) per launch, K ids uniform without "
                         f"replacement, {states} state set(s) x {len(replicas)} embedding copies",
             "results": out}
+
+
+def bench_config1(emb, e_dev, device, stream, cpu=True, states=32, launches=240):
+    """Config 1: one sequence, hidden ~N(0,1) then RMSNorm (eps 1e-5, gamma
+    ~N(1,0.02)), K = 16 allowed ids uniform without replacement, argmax over
+    the allowed logits.  CPU: the reference's own path (rms_norm_f32 + linear_f32
+    over all 49,152 rows + the masked argmax, oracle/_ref) single-threaded, and
+    the restricted-rows loop (the 16 allowed rows only); GPU: the fused
+    norm + ragged head on the same states, one state per launch (latency), 32
+    rotating states, launches in one CUDA graph.  The GPU's ids are checked
+    against the CPU path's."""
+    import torch
+
+    from market_sim_b200 import head, synth
+
+    raw = (synth.normal(80_000, 1, states * 576)).astype(np.float32).reshape(states, 576)
+    gamma = synth.normal(80_001, 2, 576, 1.0, 0.02).astype(np.float32)
+    ids = np.stack([synth.sample_without_replacement(80_002, 10 + i, 16, 49_152)
+                    for i in range(states)]).astype(np.int32)
+    out = {"workload": "1 sequence, RMSNorm'd hidden, K = 16 uniform ids, 49,152 x 576 embedding"}
+    g16 = gamma.astype(np.float16)
+    raw16 = raw.astype(np.float16)
+    h_d = [torch.from_numpy(raw16[i:i + 1]).to(device) for i in range(states)]
+    i_d = [torch.from_numpy(ids[i]).to(device) for i in range(states)]
+    off_d = torch.tensor([0, 16], dtype=torch.int32, device=device)
+    g_d = torch.from_numpy(g16).to(device)
+    o = torch.empty(1, dtype=torch.int32, device=device)
+    ws = torch.zeros(head.head_workspace_bytes(1), dtype=torch.uint8, device=device)
+    hs = stream.cuda_stream
+    got = []
+
+    def launch(i):
+        st = head.restricted_output_head_csr_rmsnorm_f16(h_d[i % states], g_d, 1e-5, e_dev, off_d,
+                                                         i_d[i % states], o, None, ws, 1, 576,
+                                                         49_152, hs)
+        if not st.ok():
+            raise RuntimeError(f"config-1 launch failed: {st}")
+
+    with torch.cuda.stream(stream):
+        for i in range(states):
+            launch(i)
+            stream.synchronize()
+            got.append(int(o.cpu().numpy().view(np.uint32)[0]))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(launches):
+                launch(i)
+        g.replay()
+        stream.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / launches
+    out["gpu_us_per_sequence"] = us
+    out["gpu_seq_per_s"] = 1e6 / us
+    if cpu:
+        from oracle import oracle as O
+
+        kind = "reference" if O.ref_available() else "port"
+        emb_f32 = O.widen(emb)
+        h16 = np.stack([O.rms_norm_f32(raw16[i:i + 1].astype(np.float32), O.widen(g16), 1e-5)
+                        .astype(np.float16)[0] for i in range(states)])
+        off = np.array([0, 16], np.int32)
+        n = 8
+        t = time.perf_counter()
+        want = []
+        for i in range(n):
+            if kind == "reference":
+                w, _ = O.ref_head_csr_by_sequence(h16[i:i + 1], emb_f32, off, ids[i], threads=1)
+            else:
+                w, _ = O.full_logits_masked_head_csr(h16[i:i + 1], emb, off, ids[i], threads=1)
+            want.append(int(w[0]))
+        dt = time.perf_counter() - t
+        t = time.perf_counter()
+        for i in range(states):
+            O.restricted_head_csr(h16[i:i + 1], emb, off, ids[i], threads=1)
+        dt_r = time.perf_counter() - t
+        out["cpu_baseline"] = {"value": n / dt, "unit": "seq/s", "cores": 1, "kind": kind,
+                               "sample": f"{n} sequences, the reference's rms_norm_f32 output "
+                                         "+ linear_f32 over all 49152 rows + masked argmax"}
+        out["cpu_restricted_rows"] = {"value": states / dt_r, "unit": "seq/s", "cores": 1,
+                                      "kind": "port",
+                                      "sample": f"{states} sequences, the 16 allowed rows only"}
+        out["ids_equal_cpu"] = int(sum(a_ == b_ for a_, b_ in zip(got[:n], want)))
+        out["ids_compared"] = n
+    return out
 
 
 REF_CELLS = [(r, k) for r in (1, 16, 256) for k in (2, 8, 32, 128)]
@@ -1133,7 +1224,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["dense", "decode", "ksweep", "rmsnorm", "market", "refgpu"],
+    ap.add_argument("--only", choices=["dense", "decode", "ksweep", "rmsnorm", "market", "refgpu",
+                                         "config1"],
                     help="run one secondary workload alone and print its result (profiling)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the dense full-vocab and DFA-decode measurements")
