@@ -76,6 +76,9 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            import atexit
+
+            atexit.register(self.__exit__, None, None, None)  # a leg that raises mid-window
             t = time.time()
             while not self.lines and time.time() - t < 5:  # first sample before timing
                 time.sleep(0.02)
@@ -88,7 +91,7 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
-        if self.proc is not None:
+        if self.proc is not None and self.proc.poll() is None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
