@@ -3,8 +3,11 @@
 //   mf_restricted_greedy_select_f16 (src/cuda/greedy.cu:61-131, 281-347)
 //   mf_greedy_select_f16            (src/cuda/greedy.cu:21-59, 237-279)
 //
-// The padded head keeps the reference's "one thread block owns one row"
-// ownership (so no cross-block merge and no workspace), but inside the block
+// The padded head keeps the reference's "one row, no workspace" contract: a
+// row is owned by one thread block, or, for long candidate tables (more than
+// 512 ids per row), by a thread-block cluster of up to 8 CTAs that split the
+// row's candidates and merge their keys through distributed shared memory
+// (still no global scratch).  Inside a block
 // the work is laid out for B200: 32 groups of 8 lanes, each group reading
 // one 1152-byte embedding row as 9 coalesced 16-byte loads per lane (two
 // rows in flight), fp16 x fp16 -> f32 FMAs, a shuffle dot reduction and a
@@ -33,17 +36,26 @@ __device__ unsigned long long block_max_key(unsigned long long k) {
   return k;  // valid in warp 0
 }
 
-template <bool kFast>
+// kCluster: launched with a cluster dimension C (grid = rows x C); CTA k of
+// the cluster takes the row's candidate groups k, k + C, ... and rank 0
+// merges the C block keys read from the peers' shared memory.
+template <bool kFast, bool kCluster = false>
 __global__ void __launch_bounds__(kRowThreads)
 padded_head_kernel(const __half* __restrict__ hidden, const __half* __restrict__ emb,
                    const uint32_t* __restrict__ allowed, const uint32_t* __restrict__ counts,
                    uint32_t* __restrict__ out, uint32_t width, uint32_t vocab, uint64_t max_allowed) {
-  const uint32_t r = blockIdx.x;
+  uint32_t crank = 0, csize = 1;
+  if (kCluster) {
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+    asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+  }
+  const uint32_t r = blockIdx.x / csize;
   const uint64_t n = counts[r];
   const bool row_bad = n == 0 || n > max_allowed;
   const int lane = threadIdx.x & 31, sub = lane & 7;
   const unsigned gmask = 0xFFu << (lane & ~7);
-  const int g = threadIdx.x >> 3;
+  const int g = (int)(crank * kRowGroups) + (threadIdx.x >> 3);  // group within the row's cluster
+  const uint64_t gstride = (uint64_t)kRowGroups * csize;
   const uint32_t* cand = allowed + (uint64_t)r * max_allowed;
   unsigned long long best = 0ull;
   if (!row_bad) {
@@ -53,10 +65,10 @@ padded_head_kernel(const __half* __restrict__ hidden, const __half* __restrict__
 #pragma unroll
       for (int k = 0; k < kFastChunksPerLane; ++k) h[k] = ld_v4(hr + sub + 8 * k);
     }
-    for (uint64_t i = g; i < n; i += 2 * kRowGroups) {
-      const bool two = i + kRowGroups < n;
+    for (uint64_t i = g; i < n; i += 2 * gstride) {
+      const bool two = i + gstride < n;
       const uint32_t t0 = cand[i];
-      const uint32_t t1 = two ? cand[i + kRowGroups] : 0u;
+      const uint32_t t1 = two ? cand[i + gstride] : 0u;
       const bool v0 = t0 < vocab, v1 = two && t1 < vocab;
       float s0 = 0.f, s1 = 0.f;
       if (kFast) {
@@ -99,6 +111,27 @@ padded_head_kernel(const __half* __restrict__ hidden, const __half* __restrict__
     }
   }
   best = block_max_key(best);
+  if (kCluster) {
+    // merge the cluster's block keys in rank 0 through distributed shared
+    // memory; the second barrier keeps every peer's key alive until read
+    __shared__ unsigned long long s_key;
+    if (threadIdx.x == 0) s_key = best;
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+    if (crank == 0 && threadIdx.x == 0) {
+      const uint32_t local = (uint32_t)__cvta_generic_to_shared(&s_key);
+      for (uint32_t q = 1; q < csize; ++q) {
+        uint32_t remote;
+        unsigned long long k;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(q));
+        asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(k) : "r"(remote) : "memory");
+        best = umax64(best, k);
+      }
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+    if (crank != 0) return;
+  }
   if (threadIdx.x == 0) out[r] = (!row_bad && key_is_result(best)) ? key_id(best) : kInvalid;
 }
 
@@ -252,15 +285,44 @@ extern "C" mf_status mf_restricted_output_head_f16(
   const bool fast = hidden_size == (uint64_t)kFastHidden && (uintptr_t)hidden % 16 == 0 &&
                     (uintptr_t)embedding % 16 == 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto args = [&](auto kernel) {
-    kernel<<<(unsigned)rows, kRowThreads, 0, s>>>(
-        static_cast<const __half*>(hidden), static_cast<const __half*>(embedding),
-        static_cast<const uint32_t*>(allowed), static_cast<const uint32_t*>(counts),
-        static_cast<uint32_t*>(token_ids), (uint32_t)hidden_size, (uint32_t)vocab, max_allowed);
-  };
-  if (fast)
-    args(padded_head_kernel<true>);
-  else
-    args(padded_head_kernel<false>);
-  return launch_status(cudaGetLastError());
+  // Long tables: a cluster of C CTAs per row, C = 512 ids per CTA rounded up
+  // to a power of two, at most 8 (portable cluster size); grid = rows x C.
+  uint32_t c = 1;
+  while (c < 8 && (uint64_t)c * 512 < max_allowed) c *= 2;
+  if (c > 1 && (uint64_t)rows * c > (uint64_t)INT32_MAX) c = 1;
+  if (c == 1) {
+    auto args = [&](auto kernel) {
+      kernel<<<(unsigned)rows, kRowThreads, 0, s>>>(
+          static_cast<const __half*>(hidden), static_cast<const __half*>(embedding),
+          static_cast<const uint32_t*>(allowed), static_cast<const uint32_t*>(counts),
+          static_cast<uint32_t*>(token_ids), (uint32_t)hidden_size, (uint32_t)vocab, max_allowed);
+    };
+    if (fast)
+      args(padded_head_kernel<true>);
+    else
+      args(padded_head_kernel<false>);
+    return launch_status(cudaGetLastError());
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(rows * c), 1, 1);
+  cfg.blockDim = dim3(kRowThreads, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = c;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const __half* hp = static_cast<const __half*>(hidden);
+  const __half* ep = static_cast<const __half*>(embedding);
+  const uint32_t* ap = static_cast<const uint32_t*>(allowed);
+  const uint32_t* cp = static_cast<const uint32_t*>(counts);
+  uint32_t* op = static_cast<uint32_t*>(token_ids);
+  cudaError_t e = fast ? cudaLaunchKernelEx(&cfg, padded_head_kernel<true, true>, hp, ep, ap, cp,
+                                            op, (uint32_t)hidden_size, (uint32_t)vocab, max_allowed)
+                       : cudaLaunchKernelEx(&cfg, padded_head_kernel<false, true>, hp, ep, ap, cp,
+                                            op, (uint32_t)hidden_size, (uint32_t)vocab, max_allowed);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return launch_status(e);
 }

@@ -370,6 +370,44 @@ def test_padded_matches_csr(mf, emb_full):
     assert np.array_equal(_u32(out), got)
 
 
+@pytest.mark.parametrize("rows,kmax,pad", [(64, 4096, 4096), (3, 2000, 1500), (1, 49_152, 49_152)])
+def test_padded_long_tables_match_csr(mf, emb_full, rows, kmax, pad):
+    """Tables of more than 512 ids per row go to a cluster of CTAs per row
+    (keys merged through distributed shared memory): the same ids as the
+    ragged head, and rows whose count is 0 or above the table width give the
+    sentinel."""
+    import torch
+
+    e, e_dev = emb_full
+    if kmax >= 49_152:
+        from market_sim_b200 import synth
+
+        h = synth.hidden_states(41, rows)
+        off = np.array([0, 49_152], np.int32)
+        ids = np.arange(49_152, dtype=np.int32)
+    else:
+        h, off, ids = _ragged_case(41 + rows, rows, kmax)
+    counts = np.diff(off).astype(np.uint32)
+    width = max(pad, int(counts.max()))
+    allowed = np.zeros((rows, width), np.uint32)
+    for r in range(rows):
+        allowed[r, :counts[r]] = ids[off[r]:off[r + 1]]
+    bad_counts = counts.copy()
+    if rows > 2:
+        bad_counts[0] = 0
+        bad_counts[1] = width + 1
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    assert mf.restricted_output_head_f16(to_dev(h), e_dev, to_dev(allowed), to_dev(bad_counts),
+                                         out, rows, 576, e.shape[0], width, _stream()).ok()
+    got = _u32(out)
+    want, _, _ = _csr_call(mf, h, e_dev, off, ids)
+    if rows > 2:
+        assert got[0] == INVALID and got[1] == INVALID
+        assert np.array_equal(got[2:], want[2:])
+    else:
+        assert np.array_equal(got, want)
+
+
 def test_host_pipeline_matches_direct_calls(mf, emb_full):
     """head.HostPipeline (pinned host in/out, overlapped copies) returns the
     same ids and scores as direct device calls, batch after batch."""
