@@ -478,15 +478,31 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       const uint32_t want = epoch & 0x7FFFFFFFu;
       const bool own_fail = s_xfail != 0u;
       const size_t par_off = kXSlots + (size_t)(epoch & 1u) * p.world * p.rows * 8;
-      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
-        const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
-        if (failed) p.keys[r] = 0ull;
-        for (uint32_t q = 0; q < p.world; ++q)
-          reinterpret_cast<unsigned long long*>(p.xbuf[q] + par_off)[(size_t)p.rank * p.rows + r] = key;
+      // every CTA's merge is complete and visible (done counter + fences):
+      // plain L2 loads, four rows per thread in flight, then the clears
+      for (uint32_t r0 = threadIdx.x; r0 < p.rows; r0 += 4 * kThreads) {
+        unsigned long long k[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t r = r0 + j * kThreads;
+          k[j] = (r < p.rows && !failed) ? __ldcg(p.keys + r) : kKeyPoison;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t r = r0 + j * kThreads;
+          if (r >= p.rows) break;
+          p.keys[r] = 0ull;
+          for (uint32_t q = 0; q < p.world; ++q)
+            reinterpret_cast<unsigned long long*>(p.xbuf[q] + par_off)[(size_t)p.rank * p.rows + r] =
+                k[j];
+        }
       }
-      __threadfence_system();
+      // the block barrier orders every thread's peer stores before the flag
+      // writers' system-scope fence and release (one fence per flag, not
+      // one per thread)
       __syncthreads();
       if (threadIdx.x < p.world) {  // this rank's flag for this call, in every buffer
+        __threadfence_system();
         uint32_t* flag = reinterpret_cast<uint32_t*>(p.xbuf[threadIdx.x] + kXFlags) + p.rank;
         const uint32_t v = (want << 1) | (own_fail ? 1u : 0u);
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
@@ -514,16 +530,13 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       if (threadIdx.x == 0 && p.error_out) *p.error_out = xfail ? 1u : 0u;
       const unsigned long long* slots =
           reinterpret_cast<const unsigned long long*>(self + par_off);
+      // ordered after the flags' acquire loads by the barrier above; L2
+      // loads (not L1: a slot parity is reused every other call), all of a
+      // row's slots in flight at once
       for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
         unsigned long long key = 0ull;
-        for (uint32_t q = 0; q < p.world; ++q) {
-          unsigned long long k;
-          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
-                       : "=l"(k)
-                       : "l"(slots + (size_t)q * p.rows + r)
-                       : "memory");
-          key = k > key ? k : key;
-        }
+#pragma unroll 8
+        for (uint32_t q = 0; q < p.world; ++q) key = umax64(key, __ldcg(slots + (size_t)q * p.rows + r));
         if (xfail) key = kKeyPoison;
         if (p.out_keys) p.out_keys[r] = key;
         if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
@@ -536,13 +549,24 @@ dense_head_kernel(const __grid_constant__ CUtensorMap tm_hidden,
       }
     } else {
       if (threadIdx.x == 0 && p.error_out) *p.error_out = failed ? 1u : 0u;
-      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
-        const unsigned long long key = failed ? kKeyPoison : atomicExch(p.keys + r, 0ull);
-        if (failed) p.keys[r] = 0ull;
-        if (p.out_keys) p.out_keys[r] = key;
-        if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
-        if (p.out_scores)
-          p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+      for (uint32_t r0 = threadIdx.x; r0 < p.rows; r0 += 4 * kThreads) {
+        unsigned long long k[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t r = r0 + j * kThreads;
+          k[j] = (r < p.rows && !failed) ? __ldcg(p.keys + r) : kKeyPoison;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t r = r0 + j * kThreads;
+          if (r >= p.rows) break;
+          p.keys[r] = 0ull;
+          const unsigned long long key = k[j];
+          if (p.out_keys) p.out_keys[r] = key;
+          if (p.out_ids) p.out_ids[r] = key_is_result(key) ? key_id(key) : kInvalid;
+          if (p.out_scores)
+            p.out_scores[r] = key_is_result(key) ? key_score(key) : __uint_as_float(0x7FC00000u);
+        }
       }
     }
     __syncthreads();
