@@ -167,8 +167,12 @@ MF_API mf_status mf_head_restricted_csr_rmsnorm_f16(
  * chosen token to out_tokens[b] and the next state to states_out[b]
  * (TokenDfa::advance, src/grammar/token_dfa.cpp:111-128).  A sequence whose
  * state is out of range or has no arcs gets MF_INVALID_TOKEN and keeps its
- * state.  The workspace rule is the same as for the CSR head, sized by
- * mf_dfa_workspace_bytes(batch). */
+ * state.  The workspace rule is the same as for the CSR head: one step needs
+ * mf_head_workspace_bytes(batch) bytes, mf_dfa_decode_f16 needs
+ * mf_dfa_workspace_bytes(batch) (three more 8-byte words per sequence: with a
+ * vocabulary of at most 65,536 ids and fewer than 65,535 states, a step hands
+ * its results to the next through rotating key buffers instead of per-row
+ * arrival counters). */
 MF_API uint64_t mf_dfa_workspace_bytes(uint64_t batch);
 
 MF_API mf_status mf_dfa_head_step_f16(const void* hidden, uint64_t hidden_bytes,

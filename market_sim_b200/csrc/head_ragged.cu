@@ -50,6 +50,19 @@ struct RaggedParams {
   // row's finaliser needs no table loads (arcs are sorted by token, so the
   // lowest token is the lowest position: the selection order is the same).
   uint32_t dfa_packed;
+  // Multi-step decode with packed keys (mf_dfa_decode_f16): a step's rows
+  // merge into dfa_keys_out by atomicMax alone (no arrival counters, no
+  // finaliser); the next step's prologue decodes them into the previous
+  // step's token / score / state rows.  Three key buffers rotate: step s
+  // writes K[s % 3], reads K[(s - 1) % 3] and clears K[(s + 1) % 3], which
+  // step s - 1's prologue has finished reading.  Null: the per-row merge.
+  unsigned long long* dfa_keys_out;
+  const unsigned long long* dfa_keys_in;  // the previous step's keys, or null (first step)
+  unsigned long long* dfa_keys_clear;
+  const uint32_t* states_prev;   // the previous step's input states
+  uint32_t* states_in_w;         // this step's input state row (written from the keys)
+  uint32_t* prev_out_ids;        // the previous step's token row
+  float* prev_out_scores;        // the previous step's score row, or null
   int64_t num_arcs;
   // outputs
   uint32_t* out_ids;
@@ -267,6 +280,12 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
                           int64_t row_b, int64_t row_e, unsigned long long key, int64_t n,
                           int sub, const BlockSlots& bs) {
   if (sub != 0 || n <= 0) return;
+  if constexpr (M == RowMode::kDfa) {
+    if (p.dfa_keys_out != nullptr) {  // decoded by the next step's prologue
+      if (key != kKeyNone) atomicMax(p.dfa_keys_out + r, key);
+      return;
+    }
+  }
   pdl_wait();  // the workspace and outputs may still belong to the previous launch
   const int64_t row_len = row_e - row_b;
   if (n == row_len) {  // the group saw the whole row: no merge needed
@@ -643,7 +662,24 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     // same table).  Invalid states and empty sets get the sentinel.
     const uint32_t rows = p.rows;
     for (uint32_t r = threadIdx.x; r < rows; r += kThreads) {
-      const uint32_t st = p.states_in[r];
+      const bool owner = (r % gridDim.x) == blockIdx.x;
+      uint32_t st;
+      if (p.dfa_keys_in != nullptr) {
+        // the previous step's result for row r, from its merged key: token
+        // and next state packed in the id; no result keeps the state
+        const unsigned long long k = __ldcg(p.dfa_keys_in + r);
+        const uint32_t sp = p.states_prev[r];
+        const bool res = key_is_result(k);
+        st = res ? (key_id(k) & 0xFFFFu) : sp;
+        if (owner) {
+          p.prev_out_ids[r] = res ? key_id(k) >> 16 : kInvalid;
+          if (p.prev_out_scores) p.prev_out_scores[r] = res ? key_score(k) : __uint_as_float(0x7FC00000u);
+          p.states_in_w[r] = st;
+        }
+      } else {
+        st = p.states_in[r];
+      }
+      if (p.dfa_keys_out != nullptr && owner) p.dfa_keys_clear[r] = 0ull;
       int32_t len = 0, base = 0;
       if (st < p.num_states) {
         const int32_t b = p.state_offsets[st], e = p.state_offsets[st + 1];
@@ -651,7 +687,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
       }
       smem_rows[r + 1] = len;
       smem_rows[rows + 1 + r] = base;
-      if (len == 0 && (r % gridDim.x) == blockIdx.x) {
+      if (len == 0 && owner && p.dfa_keys_out == nullptr) {  // (keys mode: key 0 says so)
         p.out_ids[r] = kInvalid;
         p.states_out[r] = st;
         if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
@@ -875,6 +911,25 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   }
 }
 
+// The last step of a packed-key decode: its keys to the token / score /
+// state rows, and every key buffer back to zero.
+__global__ void dfa_finish_kernel(const unsigned long long* keys, const uint32_t* states_prev,
+                                  uint32_t* out_ids, float* out_scores, uint32_t* states_out,
+                                  unsigned long long* k0, unsigned long long* k1,
+                                  unsigned long long* k2, uint32_t rows) {
+  pdl_wait();
+  const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const unsigned long long k = keys[r];
+  const bool res = key_is_result(k);
+  out_ids[r] = res ? key_id(k) >> 16 : kInvalid;
+  if (out_scores) out_scores[r] = res ? key_score(k) : __uint_as_float(0x7FC00000u);
+  states_out[r] = res ? (key_id(k) & 0xFFFFu) : states_prev[r];
+  k0[r] = 0ull;
+  k1[r] = 0ull;
+  k2[r] = 0ull;
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 
@@ -959,7 +1014,10 @@ extern "C" uint64_t mf_head_workspace_bytes(uint64_t rows) {
   return (b + 15) & ~15ull;
 }
 
-extern "C" uint64_t mf_dfa_workspace_bytes(uint64_t batch) { return mf_head_workspace_bytes(batch); }
+// the head's workspace, then three key buffers of the packed-key decode
+extern "C" uint64_t mf_dfa_workspace_bytes(uint64_t batch) {
+  return mf_head_workspace_bytes(batch) + 3 * batch * 8;
+}
 
 namespace {
 
@@ -1165,7 +1223,7 @@ static mf_status dfa_step(
   if (st.code != MF_OK) return st;
   if (states_in_bytes != batch * 4 || states_out_bytes != batch * 4 ||
       out_tokens_bytes != batch * 4 || (out_scores && out_scores_bytes != batch * 4) ||
-      workspace_bytes < mf_dfa_workspace_bytes(batch) ||
+      workspace_bytes < mf_head_workspace_bytes(batch) ||  // one step: no key buffers
       !distinct({states_in, states_out, out_tokens, workspace, hidden, embedding}) ||
       (out_scores && !distinct({out_scores, states_in, states_out, out_tokens, workspace})))
     return fail(MF_INVALID_ARGUMENT);
@@ -1249,6 +1307,14 @@ extern "C" mf_status mf_dfa_decode_f16(
     return fail(MF_INVALID_ARGUMENT);
   const bool fast = fast_path(hidden, embedding, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // packed keys (16-bit vocabulary and grammar): steps hand their results on
+  // through three rotating key buffers after the head's workspace
+  const bool packed = vocab <= 65536u && num_states < 65535u;
+  unsigned long long* kbuf[3];
+  for (int i = 0; i < 3; ++i)
+    kbuf[i] = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) +
+                                                    mf_head_workspace_bytes(batch)) +
+              (size_t)i * batch;
   for (uint64_t step = 0; step < steps; ++step) {
     RaggedParams p{};
     p.hidden = static_cast<const __half*>(hidden) + step * batch * hidden_size;
@@ -1265,9 +1331,42 @@ extern "C" mf_status mf_dfa_decode_f16(
     p.rows = (uint32_t)batch;
     p.hidden_size = (uint32_t)hidden_size;
     p.vocab = (uint32_t)vocab;
-    p.dfa_packed = vocab <= 65536u && num_states < 65535u ? 1u : 0u;
+    p.dfa_packed = packed ? 1u : 0u;
     split_workspace(workspace, batch, p);
+    if (packed) {
+      p.dfa_keys_out = kbuf[step % 3];
+      p.dfa_keys_clear = kbuf[(step + 1) % 3];
+      if (step > 0) {
+        p.dfa_keys_in = kbuf[(step - 1) % 3];
+        p.states_prev = static_cast<const uint32_t*>(state_trace) + (step - 1) * batch;
+        p.states_in_w = static_cast<uint32_t*>(state_trace) + step * batch;
+        p.prev_out_ids = static_cast<uint32_t*>(token_trace) + (step - 1) * batch;
+        p.prev_out_scores =
+            score_trace ? static_cast<float*>(score_trace) + (step - 1) * batch : nullptr;
+      }
+    }
     const cudaError_t e = dfa_launch(p, fast, s, step > 0);
+    if (e != cudaSuccess) return launch_status(e);
+  }
+  if (packed) {  // the last step's keys, decoded as the next step would have
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((batch + 255) / 256), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const uint64_t last = steps - 1;
+    cudaError_t e = cudaLaunchKernelEx(
+        &cfg, dfa_finish_kernel, (const unsigned long long*)kbuf[last % 3],
+        static_cast<const uint32_t*>(state_trace) + last * batch,
+        static_cast<uint32_t*>(token_trace) + last * batch,
+        score_trace ? static_cast<float*>(score_trace) + last * batch : (float*)nullptr,
+        static_cast<uint32_t*>(state_trace) + steps * batch, kbuf[0], kbuf[1], kbuf[2],
+        (uint32_t)batch);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return launch_status(e);
   }
   return ok();

@@ -47,6 +47,7 @@ Status restricted_output_head_f16(const DeviceBuffer& hidden, const DeviceBuffer
 Result<DeviceBuffer> allocate_head_workspace(std::uint64_t rows, StreamHandle stream) noexcept {
   std::uint64_t bytes = mf_head_workspace_bytes(rows);
   if (mf_dense_workspace_bytes(rows) > bytes) bytes = mf_dense_workspace_bytes(rows);
+  if (mf_dfa_workspace_bytes(rows) > bytes) bytes = mf_dfa_workspace_bytes(rows);
   auto buf = DeviceBuffer::allocate(bytes);
   if (!buf) return buf;
   const auto e = cudaMemsetAsync(reinterpret_cast<void*>(buf.value().address().value), 0,

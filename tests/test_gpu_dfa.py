@@ -39,7 +39,7 @@ def _decode(mf, hidden, e_dev, off, tok, nxt, init, num_states):
     trace[0] = to_dev(init.astype(np.int32))
     tokens = torch.empty((steps, batch), dtype=torch.int32, device="cuda")
     scores = torch.empty((steps, batch), dtype=torch.float32, device="cuda")
-    ws = torch.zeros(mf.head_workspace_bytes(batch), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(mf.dfa_workspace_bytes(batch), dtype=torch.uint8, device="cuda")
     st = mf.dfa_decode_f16(to_dev(hidden), e_dev, to_dev(off), to_dev(tok.astype(np.int32)),
                            to_dev(nxt.astype(np.int32)), trace, tokens, scores, ws, steps, batch,
                            num_states, hs, int(e_dev.shape[0]), _stream())
