@@ -141,3 +141,40 @@ def test_market_dfa_decode_walks_the_grammar(mf, O, golden_dir, cuda):
     # market-DFA fan-out is at most 11, so near-ties are vanishingly rare
     assert np.array_equal(g_tok, o_tok)
     assert np.array_equal(g_states, o_states)
+
+
+@pytest.mark.parametrize("steps", [1, 2, 3, 7])
+def test_decode_key_hand_on_matches_single_steps(mf, steps):
+    """mf_dfa_decode_f16 hands each step's result to the next through
+    rotating key buffers (decoded by the next step's prologue, the last by a
+    finishing kernel); the traces must equal those of the same steps run one
+    at a time through mf_dfa_head_step_f16 (per-row merge and finaliser), for
+    every step count around the three-buffer rotation, and the workspace is
+    left zero."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    ns, batch = 16, 48
+    e = synth.embedding(515, vocab=8192)
+    e_dev = to_dev(e)
+    off, tok, nxt = synth.synthetic_dfa(515, num_states=ns, kmax=700, vocab=8192)
+    hidden = synth.decode_hidden(516, steps, batch)
+    init = (np.arange(batch) * 5 % ns).astype(np.uint32)
+    g_tok, g_states, g_sc = _decode(mf, hidden, e_dev, off, tok, nxt, init, ns)
+    off_d, tok_d, nxt_d = to_dev(off), to_dev(tok.astype(np.int32)), to_dev(nxt.astype(np.int32))
+    ws = torch.zeros(mf.head_workspace_bytes(batch), dtype=torch.uint8, device="cuda")
+    state = to_dev(init.astype(np.int32))
+    for s in range(steps):
+        nstate = torch.empty(batch, dtype=torch.int32, device="cuda")
+        out = torch.empty(batch, dtype=torch.int32, device="cuda")
+        sc = torch.empty(batch, dtype=torch.float32, device="cuda")
+        st = mf.dfa_head_step_f16(to_dev(hidden[s]), e_dev, off_d, tok_d, nxt_d, state, nstate, out,
+                                  sc, ws, batch, ns, 576, 8192, gpu_stream())
+        assert st.ok(), st
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), g_tok[s]), s
+        assert np.array_equal(nstate.cpu().numpy().view(np.uint32), g_states[s + 1]), s
+        np.testing.assert_array_equal(sc.cpu().numpy().view(np.uint32), g_sc[s].view(np.uint32))
+        state = nstate
+    assert int(ws.sum()) == 0
