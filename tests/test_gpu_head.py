@@ -603,3 +603,26 @@ def test_overlapped_launches_match_plain_calls(mf, emb_full):
     assert np.array_equal(_u32(outs[0][0]), want[0][0])
     assert np.array_equal(_u32(outs[1][0]), want[1][0])
     assert int(ws.sum()) == 0
+
+
+def test_padded_long_table_generic_width(mf):
+    """The cluster-split padded head on the generic (non-576) path: a
+    64-wide model, 1,500-id tables, equals the ragged head."""
+    import torch
+
+    from market_sim_b200 import synth
+
+    v, hs, rows = 3000, 64, 5
+    e = synth.embedding(77, vocab=v, hidden=hs)
+    e_dev = to_dev(e)
+    h = synth.hidden_states(78, rows, hs)
+    off, ids = synth.ragged_batch(79, rows=rows, kmax=1500, vocab=v)
+    counts = np.diff(off).astype(np.uint32)
+    allowed = np.zeros((rows, 1500), np.uint32)
+    for r in range(rows):
+        allowed[r, :counts[r]] = ids[off[r]:off[r + 1]]
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    assert mf.restricted_output_head_f16(to_dev(h), e_dev, to_dev(allowed), to_dev(counts), out,
+                                         rows, hs, v, 1500, _stream()).ok()
+    want, _, _ = _csr_call(mf, h, e_dev, off, ids)
+    assert np.array_equal(_u32(out), want)
