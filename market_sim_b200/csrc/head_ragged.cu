@@ -288,7 +288,12 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
   }
   pdl_wait();  // the workspace and outputs may still belong to the previous launch
   const int64_t row_len = row_e - row_b;
-  if (n == row_len) {  // the group saw the whole row: no merge needed
+  // Batches of up to kLocalCheckRows rows: the block's part of the row goes
+  // to the row key by one atomicMax and nothing waits on it; the finishing
+  // kernel decodes every key after the whole grid (no arrival counter, no
+  // finaliser on the critical path of a block).
+  const bool keys_only = M == RowMode::kCsr && p.rows <= kLocalCheckRows;
+  if (n == row_len && !keys_only) {  // the group saw the whole row: no merge needed
     finalize_row<M>(p, rows_tab, r, key);
     return;
   }
@@ -303,10 +308,14 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
     __threadfence_block();
     key = atomicExch(bs.key + slot, 0ull);
     n = local;
-    if (n == row_len) {  // the row lies inside this block
+    if (n == row_len && !keys_only) {  // the row lies inside this block
       finalize_row<M>(p, rows_tab, r, key);
       return;
     }
+  }
+  if (keys_only) {
+    if (key != kKeyNone) atomicMax(p.keys + r, key);
+    return;
   }
   if (key != kKeyNone) atomicMax(p.keys + r, key);
   const uint32_t before = arrive_acq_rel(p.counts + r, (uint32_t)n);
@@ -315,6 +324,48 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
     p.counts[r] = 0u;
     finalize_row<M>(p, rows_tab, r, merged);
   }
+}
+
+// Batches of up to kLocalCheckRows rows: one pass of the block over the
+// offsets.  It checks them (non-decreasing, offsets[0] = 0, offsets[rows] =
+// total) and counts how many rows start at or before the block's first and
+// last candidate, which gives the rows [first, last] that the block's range
+// [b_begin, b_end) covers without a search.  false: malformed (the whole
+// block returns; every block finds the same, so no block merges a key and the
+// finishing kernel gives every row the sentinel).
+__device__ __forceinline__ bool csr_local_check(const RaggedParams& p, int64_t b_begin,
+                                                int64_t b_end, uint32_t (*s_row_counts)[2],
+                                                uint32_t& first, uint32_t& last) {
+  const int64_t b0 = b_begin, b1 = b_end - 1;
+  int bad = 0;
+  uint32_t n0 = 0, n1 = 0;
+  for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+    const int32_t o = __ldg(p.offsets + r);
+    bad |= o > __ldg(p.offsets + r + 1);
+    n0 += (int64_t)o <= b0;
+    n1 += (int64_t)o <= b1;
+  }
+  if (threadIdx.x == 0)
+    bad |= __ldg(p.offsets) != 0 || (int64_t)__ldg(p.offsets + p.rows) != p.total;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    n0 += __shfl_xor_sync(0xFFFFFFFFu, n0, o);
+    n1 += __shfl_xor_sync(0xFFFFFFFFu, n1, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_row_counts[threadIdx.x >> 5][0] = n0;
+    s_row_counts[threadIdx.x >> 5][1] = n1;
+  }
+  if (__syncthreads_or(bad)) return false;
+  n0 = n1 = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) {
+    n0 += s_row_counts[w][0];
+    n1 += s_row_counts[w][1];
+  }
+  first = n0 > 0 ? n0 - 1 : 0u;
+  last = n1 > 0 ? n1 - 1 : 0u;
+  return true;
 }
 
 // 16-byte asynchronous global -> shared copy (no registers on the way) and
@@ -420,8 +471,8 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
                                                int64_t c_begin, int64_t c_end, int sub,
                                                unsigned gmask, uint4* slot,
                                                const BlockSlots& bs, BlockRowTable& tab,
-                                               uint32_t* s_rows_found, bool rows_known,
-                                               uint32_t known_first, uint32_t known_last) {
+                                               uint32_t* s_rows_found,
+                                               uint32_t (*s_row_counts)[2]) {
   const uint4* emb = reinterpret_cast<const uint4*>(p.embedding);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int64_t c = c_begin;
@@ -448,7 +499,15 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
   if (c < c_end) issue();
 
   // ---- the block's rows: [first, last] covering [bs.begin, bs.end) ----
-  // (small batches: counted by the kernel's offset check on entry)
+  // (small batches: counted by the offset check, whose loads overlap the
+  // first embedding loads; the candidate indices are below total whatever
+  // the offsets hold, so those loads stay in bounds)
+  bool rows_known = false;
+  uint32_t known_first = 0, known_last = 0;
+  if (p.rows <= kLocalCheckRows) {
+    if (!csr_local_check(p, bs.begin, bs.end, s_row_counts, known_first, known_last)) return;
+    rows_known = true;
+  }
   if (!rows_known) {
     if (warp == 0 && lane < 16) {  // group 0: first row, group 1: last row
       const int64_t at = lane < 8 ? bs.begin : bs.end - 1;
@@ -600,8 +659,6 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   Rows<M> rows_tab;
   int64_t total;
   __shared__ uint32_t s_row_counts[kThreads / 32][2];
-  bool rows_known = false;  // CSR, small batches: the block's first and last rows
-  uint32_t known_first = 0, known_last = 0;
   if (M == RowMode::kCsr) {
     // Overlapped launches: the next batch's blocks may start as this one's
     // retire.  Reads of this call's inputs need no wait (the caller promises
@@ -610,49 +667,13 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     pdl_trigger();
     rows_tab.start = p.offsets;
     total = p.total;
-    if (p.rows <= kLocalCheckRows) {
-      // One pass over the offsets: the check, and (fast path) how many
-      // rows start at or before the block's first and last candidate,
-      // which gives the rows the block covers without a search.
-      const int64_t b0 = min(p.total, (int64_t)blockIdx.x * kGroupsPerBlock * chunk);
-      const int64_t b1 = min(p.total, b0 + (int64_t)kGroupsPerBlock * chunk) - 1;
-      int bad = 0;
-      uint32_t n0 = 0, n1 = 0;
-      for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
-        const int32_t o = __ldg(p.offsets + r);
-        bad |= o > __ldg(p.offsets + r + 1);
-        n0 += (int64_t)o <= b0;
-        n1 += (int64_t)o <= b1;
-      }
-      if (threadIdx.x == 0)
-        bad |= __ldg(p.offsets) != 0 || (int64_t)__ldg(p.offsets + p.rows) != p.total;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        n0 += __shfl_xor_sync(0xFFFFFFFFu, n0, o);
-        n1 += __shfl_xor_sync(0xFFFFFFFFu, n1, o);
-      }
-      if ((threadIdx.x & 31) == 0) {
-        s_row_counts[threadIdx.x >> 5][0] = n0;
-        s_row_counts[threadIdx.x >> 5][1] = n1;
-      }
-      if (__syncthreads_or(bad)) {  // malformed: sentinel for this block's rows only
-        pdl_wait();
-        for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows;
-             r += gridDim.x * kThreads) {
-          p.out_ids[r] = kInvalid;
-          if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
-        }
+    // (the fast path checks inside csr_fast_block, behind its first loads)
+    if (!kFast && p.rows <= kLocalCheckRows) {
+      uint32_t first, last;  // (only the fast path uses the block's rows)
+      if (!csr_local_check(p, min(p.total, (int64_t)blockIdx.x * kGroupsPerBlock * chunk),
+                           min(p.total, (int64_t)(blockIdx.x + 1) * kGroupsPerBlock * chunk),
+                           s_row_counts, first, last))
         return;
-      }
-      n0 = n1 = 0;
-#pragma unroll
-      for (int w = 0; w < kThreads / 32; ++w) {
-        n0 += s_row_counts[w][0];
-        n1 += s_row_counts[w][1];
-      }
-      rows_known = true;
-      known_first = n0 > 0 ? n0 - 1 : 0u;
-      known_last = n1 > 0 ? n1 - 1 : 0u;
     }
   } else {
     pdl_trigger();  // the next decode step's blocks may queue behind this one's
@@ -753,7 +774,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     tab.start = s_tab_start;
     csr_fast_block<kNorm>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
                           c_end, sub, gmask, s_hid + threadIdx.x, bs, tab, s_rows_found,
-                          rows_known, known_first, known_last);
+                          s_row_counts);
   } else if (c_begin < c_end) {
     uint32_t r = find_row<M>(rows_tab, p.rows, c_begin, sub, gmask);
     int64_t row_b = rows_tab.at(r);
@@ -852,17 +873,11 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   }
 
   if constexpr (M == RowMode::kDfa) return;
+  // Offsets checked on entry: the finishing kernel decodes every row key
+  // (an empty row's key is zero, which decodes to the sentinel).
+  if (p.rows <= kLocalCheckRows) return;
   // Empty rows get the sentinel here (no group visits them).
   pdl_wait();
-  if (p.rows <= kLocalCheckRows) {  // offsets checked on entry: no flag, no arrival counter
-    for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += gridDim.x * kThreads) {
-      if (p.offsets[r] == p.offsets[r + 1]) {
-        p.out_ids[r] = kInvalid;
-        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
-      }
-    }
-    return;
-  }
   // Larger batches: decreasing offsets or a bad first/last offset flag the
   // batch for the last block out.
   for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += gridDim.x * kThreads) {
@@ -909,6 +924,22 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
       p.control[0] = 0u;
     }
   }
+}
+
+// CSR batches of up to kLocalCheckRows rows: after the whole head grid (a
+// programmatic dependent launch that waits for it), every row key to the id
+// and score rows, and the key back to zero for the next call.
+__global__ void csr_finish_kernel(unsigned long long* keys, uint32_t* out_ids, float* out_scores,
+                                  uint32_t rows) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const unsigned long long k = keys[r];
+  keys[r] = 0ull;
+  const bool res = key_is_result(k);
+  out_ids[r] = res ? key_id(k) : kInvalid;
+  if (out_scores) out_scores[r] = res ? key_score(k) : __uint_as_float(0x7FC00000u);
 }
 
 // The last step of a packed-key decode: its keys to the token / score /
@@ -1108,6 +1139,19 @@ static mf_status csr_head(
   else
     e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, false>, p, chunk);
   if (e == cudaSuccess) e = cudaGetLastError();
+  if (e == cudaSuccess && rows <= (uint64_t)kLocalCheckRows) {
+    cudaLaunchConfig_t fin = {};
+    fin.gridDim = dim3((unsigned)((rows + kThreads - 1) / kThreads), 1, 1);
+    fin.blockDim = dim3(kThreads, 1, 1);
+    fin.stream = cfg.stream;
+    cudaLaunchAttribute fa[1];
+    fa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    fa[0].val.programmaticStreamSerializationAllowed = 1;
+    fin.attrs = fa;
+    fin.numAttrs = 1;
+    e = cudaLaunchKernelEx(&fin, csr_finish_kernel, p.keys, p.out_ids, p.out_scores, p.rows);
+    if (e == cudaSuccess) e = cudaGetLastError();
+  }
   return launch_status(e);
 }
 
