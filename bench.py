@@ -388,8 +388,9 @@ def run_ours(args):
                               "seq_per_s": ROWS * world / (warm_ms * 1e-3),
                               "note": "same steps, one embedding copy kept in L2 (not the "
                                       "headline value)"},
-        "gpu_launches": args.steps,
-        "timing": {"value": "CUDA graph of the K launches (each may overlap the previous "
+        # per step: the head kernel and the kernel that decodes its row keys
+        "gpu_launches": 2 * args.steps,
+        "timing": {"value": "CUDA graph of the K calls (each may overlap the previous "
                             "launch's tail: programmatic dependent launch), events around one "
                             "replay",
                    "roofline": f"{roofline_timing}, {n_ev} launches",

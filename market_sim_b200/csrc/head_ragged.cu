@@ -610,31 +610,42 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
     return true;
   };
 
+  // The next iteration's loads are issued as soon as the dot products have
+  // consumed the rows, so the group's lane reductions and key updates run
+  // while they are in flight.  Exception: the per-group fallback with the
+  // fused norm enters a new row before issuing the loads, since the
+  // normalisation needs registers that two rows in flight would occupy.
+  const bool late_issue = kNorm && !table;
   while (c < c_end) {
-    if (!pre) {
-      // the per-group fallback with the fused norm enters a new row before
-      // issuing the loads: the normalisation needs registers that two rows in
-      // flight would occupy
-      if (kNorm && !table && c >= row_e && !enter_row()) break;
+    if (!pre && late_issue) {
+      if (c >= row_e && !enter_row()) break;
       issue();
     }
     pre = false;
     if (c >= row_e && !enter_row()) break;
     const bool two = has1 && c + 1 < row_e;  // the second candidate is in this row
-    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+    // four partial sums per candidate (two per lane half of each 16-byte
+    // chunk, alternating chunks): half the FMA dependency chain
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < kFastChunksPerLane; ++k) {
       const uint4 hk = hid[k * hstride];
-      if (v0) dot_v4(a00, a01, hk, e0[k]);
-      if (v1) dot_v4(a10, a11, hk, e1[k]);
+      if (v0) dot_v4(a0[2 * (k & 1)], a0[2 * (k & 1) + 1], hk, e0[k]);
+      if (v1) dot_v4(a1[2 * (k & 1)], a1[2 * (k & 1) + 1], hk, e1[k]);
     }
-    const float s0 = group8_sum(a00 + a01, gmask);
-    const float s1 = group8_sum(a10 + a11, gmask);
-    best = umax64(best, v0 ? make_key(s0, t0) : kKeyPoison);
-    if (two) best = umax64(best, v1 ? make_key(s1, t1) : kKeyPoison);
+    const uint32_t id0 = t0, id1 = t1;
+    const bool ok0 = v0, ok1 = v1;
     const int64_t n_here = two ? 2 : 1;
     seen += n_here;
     c += n_here;
+    if (!late_issue && c < c_end) {
+      issue();
+      pre = true;
+    }
+    const float s0 = group8_sum((a0[0] + a0[1]) + (a0[2] + a0[3]), gmask);
+    const float s1 = group8_sum((a1[0] + a1[1]) + (a1[2] + a1[3]), gmask);
+    best = umax64(best, ok0 ? make_key(s0, id0) : kKeyPoison);
+    if (two) best = umax64(best, ok1 ? make_key(s1, id1) : kKeyPoison);
   }
   if (have_row) flush_row<RowMode::kCsr>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
 }
