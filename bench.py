@@ -44,7 +44,7 @@ BATCHES = 8
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one launch, from one ncu capture of the same
 # workload (dram__bytes_read.sum + dram__bytes_write.sum)
-TRAFFIC_RAGGED = 54.55e6
+TRAFFIC_RAGGED = 54.60e6
 TRAFFIC_DENSE = 60.47e6
 
 
