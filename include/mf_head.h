@@ -102,7 +102,9 @@ MF_API mf_status mf_restricted_output_head_f16(const void* hidden, uint64_t hidd
  * the whole batch are split evenly over the GPU, so one long row is shared
  * by many thread blocks; partial results merge through 64-bit atomic max on
  * a packed (score, id) key in `workspace`, which makes the result
- * independent of scheduling.
+ * independent of scheduling.  A call is two kernels on `stream`: the head,
+ * and (batches of up to 4,096 rows) a small kernel that decodes the row keys
+ * into out_ids / out_scores and clears them.
  *
  * workspace: mf_head_workspace_bytes(rows) bytes of device memory, zero-filled
  * once by the caller before its first use; every call leaves it zero again.
@@ -127,7 +129,7 @@ MF_API mf_status mf_head_restricted_csr_f16(const void* hidden, uint64_t hidden_
 /* mf_head_restricted_csr_f16 with launch options.  MF_LAUNCH_OVERLAP_PREVIOUS:
  * the launch may begin while the previous kernel on `stream` is still running
  * (programmatic dependent launch), so back-to-back batches overlap one's
- * tail with the next one's gathers.  The kernel waits for the previous
+ * tail with the next one's gathers.  The head waits for the previous
  * kernel before its first write (workspace, outputs), but reads hidden,
  * offsets, ids and the embedding without waiting: use the flag only when the
  * previous kernel on the stream does not write them (e.g. consecutive head
