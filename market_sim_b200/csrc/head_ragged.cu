@@ -456,7 +456,8 @@ __device__ __forceinline__ void stage_row_warp(const RaggedParams& p, uint32_t r
 //     once; while they are in flight the block finds the rows its range
 //     covers and, when they are at most kBlockRows, stages those hidden rows
 //     (normalised, when fusing the norm) and their offsets in shared memory
-//     once for all groups, a warp per row.
+//     once for all groups, a warp per row.  (With the fused norm the first
+//     loads wait for the staging.)
 //   * Each iteration then issues the embedding loads of its (up to) two
 //     candidates before settling which row they belong to, so a change of
 //     row (the flush of the finished row, the next row's offsets and hidden
@@ -496,7 +497,9 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
       for (int k = 0; k < kFastChunksPerLane; ++k) e1[k] = ld_stream_v4(row + 8 * k);
     }
   };
-  if (c < c_end) issue();
+  // (with the fused norm, after the staging below: the rows' normalisation
+  // needs the registers that two rows in flight would hold)
+  if (!kNorm && c < c_end) issue();
 
   // ---- the block's rows: [first, last] covering [bs.begin, bs.end) ----
   // (small batches: counted by the offset check, whose loads overlap the
@@ -528,6 +531,7 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
     if ((int)threadIdx.x <= tab.n) tab.start[threadIdx.x] = rows_tab.at(first + threadIdx.x);
   }
   __syncthreads();
+  if (kNorm && c < c_end) issue();
 
   // ---- the group's candidates ----
   const bool table = tab.n > 0;
