@@ -142,6 +142,19 @@ MF_API mf_status mf_head_restricted_csr_f16_ex(
     void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
     uint64_t vocab, uint32_t launch_flags, void* stream);
 
+/* mf_head_restricted_csr_f16_ex with the candidate ids as u16 [total_ids]
+ * (ids_bytes = 2 * total_ids), for vocabularies of at most 65,536 ids
+ * (invalid_argument otherwise; SmolLM2's is 49,152): half the bytes for a
+ * caller that moves batches from host memory.  Results are those of the
+ * int32 entry on the same ids.  No counterpart in the reference, whose ids
+ * are int32 (include/marketforge/cuda/greedy.hpp). */
+MF_API mf_status mf_head_restricted_csr_u16ids_f16_ex(
+    const void* hidden, uint64_t hidden_bytes, const void* embedding, uint64_t embedding_bytes,
+    const void* offsets, uint64_t offsets_bytes, const void* ids, uint64_t ids_bytes,
+    void* out_ids, uint64_t out_ids_bytes, void* out_scores, uint64_t out_scores_bytes,
+    void* workspace, uint64_t workspace_bytes, uint64_t rows, uint64_t hidden_size,
+    uint64_t vocab, uint32_t launch_flags, void* stream);
+
 /* The same head with the decoder's final RMSNorm fused in front: `hidden`
  * holds the last layer's un-normalised rows (fp16 [rows, hidden_size]) and
  * gamma the norm weight (fp16 [hidden_size], 16-byte aligned).  Each row is
@@ -347,6 +360,15 @@ MF_API mf_status mf_pipeline_submit(mf_pipeline* pipeline, const void* hidden, u
 MF_API mf_status mf_pipeline_submit_packed(mf_pipeline* pipeline, const void* batch,
                                            uint64_t batch_bytes, uint64_t rows,
                                            uint64_t total_ids, void* out, uint64_t* ticket);
+/* mf_pipeline_submit_packed with the ids as u16 [total_ids] (batch_bytes =
+ * rows*hidden_size*2 + (rows+1)*4 + total_ids*2), for vocabularies of at most
+ * 65,536 ids (invalid_argument otherwise): a batch's ids are most of its
+ * bytes, and the host-to-device copy bounds the pipeline.  No counterpart in
+ * the reference, whose ids are int32 (include/marketforge/cuda/greedy.hpp). */
+MF_API mf_status mf_pipeline_submit_packed_u16ids(mf_pipeline* pipeline, const void* batch,
+                                                  uint64_t batch_bytes, uint64_t rows,
+                                                  uint64_t total_ids, void* out,
+                                                  uint64_t* ticket);
 MF_API mf_status mf_pipeline_wait(mf_pipeline* pipeline, uint64_t ticket);
 MF_API mf_status mf_pipeline_synchronize(mf_pipeline* pipeline);
 /* The number of slots, and slot `slot`'s stream (NULL past the last slot). */

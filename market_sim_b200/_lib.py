@@ -38,6 +38,7 @@ _SIGNATURES = {
 
 _SIGNATURES["mf_head_restricted_csr_f16_ex"] = ([_P, _U64] * 7 + [_U64, _U64, _U64, ctypes.c_uint32,
                                                                      _P])
+_SIGNATURES["mf_head_restricted_csr_u16ids_f16_ex"] = _SIGNATURES["mf_head_restricted_csr_f16_ex"]
 _SIGNATURES["mf_head_restricted_csr_f16_noalloc"] = [_P, _U64, _P, _U64, _P, _U64, _P, _U64, _P,
                                                      _U64, _P, _U64, _U64, _U64, _U64, _P]
 
@@ -65,6 +66,7 @@ _SIGNATURES["mf_pipeline_create"] = [ctypes.POINTER(_P), _P, _U64, _U64, _U64, _
                                      ctypes.c_uint32]
 _SIGNATURES["mf_pipeline_submit"] = [_P, _P, _U64, _P, _P, _U64, _P, _P, ctypes.POINTER(_U64)]
 _SIGNATURES["mf_pipeline_submit_packed"] = [_P, _P, _U64, _U64, _U64, _P, ctypes.POINTER(_U64)]
+_SIGNATURES["mf_pipeline_submit_packed_u16ids"] = _SIGNATURES["mf_pipeline_submit_packed"]
 _SIGNATURES["mf_pipeline_wait"] = [_P, _U64]
 _SIGNATURES["mf_pipeline_synchronize"] = [_P]
 

@@ -19,6 +19,7 @@ namespace {
 
 // A slot holds one batch in the packed layout of mf_pipeline_submit_packed:
 // `in` = hidden fp16 [rows, H] | offsets int32 [rows + 1] | ids int32 [total]
+// (ids u16 [total] for mf_pipeline_submit_packed_u16ids)
 // and `out` = ids u32 [rows] | scores f32 [rows], so a packed host batch moves
 // with one copy each way.
 struct Slot {
@@ -38,8 +39,8 @@ struct mf_pipeline {
   std::vector<Slot> slots;
   uint64_t submitted = 0;
 
-  uint64_t packed_bytes(uint64_t rows, uint64_t total_ids) const {
-    return rows * hidden_size * 2 + (rows + 1) * 4 + total_ids * 4;
+  uint64_t packed_bytes(uint64_t rows, uint64_t total_ids, uint64_t id_size = 4) const {
+    return rows * hidden_size * 2 + (rows + 1) * 4 + total_ids * id_size;
   }
 };
 
@@ -87,15 +88,21 @@ void release(mf_pipeline* p) {
 // packed: two pinned allocations can be neighbours, and one copy across both
 // is invalid.
 mf_status run_and_return(mf_pipeline* p, Slot& s, uint64_t rows, uint64_t total_ids,
-                         void* out_ids, void* out_scores, bool joined, uint64_t* ticket) {
+                         void* out_ids, void* out_scores, bool joined, uint64_t* ticket,
+                         bool ids_u16 = false) {
   const uint64_t hb = rows * p->hidden_size * 2;
   char* in = static_cast<char*>(s.in);
   char* out = static_cast<char*>(s.out);
-  const mf_status h = mf_head_restricted_csr_f16(
-      in, hb, p->embedding, p->embedding_bytes, in + hb, (rows + 1) * 4,
-      total_ids ? in + hb + (rows + 1) * 4 : nullptr, total_ids * 4, out, rows * 4,
-      out + rows * 4, rows * 4, s.workspace, mf_head_workspace_bytes(rows), rows,
-      p->hidden_size, p->vocab, s.stream);
+  const void* ids = total_ids ? in + hb + (rows + 1) * 4 : nullptr;
+  const mf_status h =
+      ids_u16 ? mf_head_restricted_csr_u16ids_f16_ex(
+                    in, hb, p->embedding, p->embedding_bytes, in + hb, (rows + 1) * 4, ids,
+                    total_ids * 2, out, rows * 4, out + rows * 4, rows * 4, s.workspace,
+                    mf_head_workspace_bytes(rows), rows, p->hidden_size, p->vocab, 0u, s.stream)
+              : mf_head_restricted_csr_f16(
+                    in, hb, p->embedding, p->embedding_bytes, in + hb, (rows + 1) * 4, ids,
+                    total_ids * 4, out, rows * 4, out + rows * 4, rows * 4, s.workspace,
+                    mf_head_workspace_bytes(rows), rows, p->hidden_size, p->vocab, s.stream);
   if (h.code != MF_OK) return h;
   cudaError_t e =
       cudaMemcpyAsync(out_ids, out, rows * (joined ? 8 : 4), cudaMemcpyDeviceToHost, s.stream);
@@ -186,6 +193,24 @@ extern "C" mf_status mf_pipeline_submit_packed(mf_pipeline* p, const void* batch
   if (e != cudaSuccess) return st_rt(e);
   return run_and_return(p, s, rows, total_ids, out, static_cast<char*>(out) + rows * 4, true,
                         ticket);
+}
+
+extern "C" mf_status mf_pipeline_submit_packed_u16ids(mf_pipeline* p, const void* batch,
+                                                      uint64_t batch_bytes, uint64_t rows,
+                                                      uint64_t total_ids, void* out,
+                                                      uint64_t* ticket) {
+  if (p == nullptr || batch == nullptr || out == nullptr || rows == 0 || p->vocab > 65536)
+    return mf_status{MF_INVALID_ARGUMENT, 0};
+  if (rows > p->max_rows || total_ids > p->max_ids) return mf_status{MF_RESOURCE_LIMIT, 0};
+  if (batch_bytes != p->packed_bytes(rows, total_ids, 2)) return mf_status{MF_INVALID_ARGUMENT, 0};
+  DeviceScope scope(p->device);
+  if (scope.err != cudaSuccess) return st_rt(scope.err);
+  Slot& s = p->slots[p->submitted % p->slots.size()];
+  const cudaError_t e =
+      cudaMemcpyAsync(s.in, batch, batch_bytes, cudaMemcpyHostToDevice, s.stream);
+  if (e != cudaSuccess) return st_rt(e);
+  return run_and_return(p, s, rows, total_ids, out, static_cast<char*>(out) + rows * 4, true,
+                        ticket, true);
 }
 
 extern "C" mf_status mf_pipeline_wait(mf_pipeline* p, uint64_t ticket) {

@@ -269,6 +269,18 @@ def restricted_output_head_csr_f16_ex(hidden: Buffer, embedding: Buffer, offsets
         *_pb(workspace), rows, hidden_size, vocabulary_size, launch_flags, _sp(stream)))
 
 
+def restricted_output_head_csr_u16ids_f16_ex(hidden: Buffer, embedding: Buffer, offsets: Buffer,
+                                             ids: Buffer, token_ids: Buffer,
+                                             scores: Optional[Buffer], workspace: Buffer, rows: int,
+                                             hidden_size: int, vocabulary_size: int,
+                                             launch_flags: int, stream) -> Status:
+    """``restricted_output_head_csr_f16_ex`` with the candidate ids as uint16
+    (vocabularies of at most 65,536 ids): half the bytes to move per batch."""
+    return _status(lib.mf_head_restricted_csr_u16ids_f16_ex(
+        *_pb(hidden), *_pb(embedding), *_pb(offsets), *_pb(ids), *_pb(token_ids), *_pb(scores),
+        *_pb(workspace), rows, hidden_size, vocabulary_size, launch_flags, _sp(stream)))
+
+
 NOALLOC_MAX_ROWS = 65536
 """Largest batch ``restricted_output_head_csr_f16_noalloc`` accepts."""
 
@@ -563,12 +575,19 @@ class HostPipeline:
         return self._ticket.value
 
     @staticmethod
-    def pack(hidden, offsets, ids):
+    def pack(hidden, offsets, ids, u16_ids: bool = False):
         """One pinned uint8 host buffer holding hidden fp16 [rows, H], offsets
         int32 [rows + 1] and ids int32 [total] back to back (the layout of
-        ``submit_packed``)."""
+        ``submit_packed``); with ``u16_ids`` the ids as uint16 (the layout of
+        ``submit_packed(..., u16_ids=True)``, vocabularies of at most 65,536)."""
+        import numpy as np
         import torch
 
+        if u16_ids:
+            a = np.asarray(ids)
+            if a.size and (a.min() < 0 or a.max() > 0xFFFF):
+                raise ValueError("ids outside [0, 65535] do not fit uint16")
+            ids = torch.from_numpy(a.astype(np.uint16).view(np.int16))
         parts = [torch.as_tensor(x).contiguous().view(torch.uint8).reshape(-1)
                  for x in (hidden, offsets, ids)]
         buf = torch.empty(sum(p.numel() for p in parts), dtype=torch.uint8).pin_memory()
@@ -579,20 +598,21 @@ class HostPipeline:
         return buf
 
     def submit_packed_ptrs(self, batch: int, batch_bytes: int, rows: int, total_ids: int,
-                           out: int) -> int:
+                           out: int, u16_ids: bool = False) -> int:
         """One packed batch (see ``pack``) at host address ``batch``; ``out``
         receives ids u32 [rows] then scores f32 [rows].  One H2D and one D2H
         copy per batch."""
-        s = lib.mf_pipeline_submit_packed(self._p, batch, batch_bytes, rows, total_ids, out,
-                                          self._ticket_ref)
+        f = lib.mf_pipeline_submit_packed_u16ids if u16_ids else lib.mf_pipeline_submit_packed
+        s = f(self._p, batch, batch_bytes, rows, total_ids, out, self._ticket_ref)
         if s.code:
             raise RuntimeError(f"mf_pipeline_submit_packed failed: {_status(s)}")
         return self._ticket.value
 
-    def submit_packed(self, batch, rows: int, total_ids: int, out) -> int:
-        """``batch`` from ``pack``; ``out`` a pinned host tensor of 8 * rows bytes."""
+    def submit_packed(self, batch, rows: int, total_ids: int, out, u16_ids: bool = False) -> int:
+        """``batch`` from ``pack`` (with the same ``u16_ids``); ``out`` a pinned
+        host tensor of 8 * rows bytes."""
         return self.submit_packed_ptrs(batch.data_ptr(), batch.numel() * batch.element_size(),
-                                       rows, total_ids, out.data_ptr())
+                                       rows, total_ids, out.data_ptr(), u16_ids)
 
     def wait(self, ticket: int) -> None:
         st = _status(lib.mf_pipeline_wait(self._p, ticket))

@@ -183,3 +183,24 @@ def test_dfa_rmsnorm_step_rejections(lib):
     assert call(gamma=0) == E.invalid_argument  # the norm weight aliases the hidden rows
     assert call(batch=0) == E.invalid_argument
     assert call(stream=0) == E.invalid_argument
+
+
+def test_csr_u16ids_rejections(lib):
+    """mf_head_restricted_csr_u16ids_f16_ex: the ids are u16, so a vocabulary
+    above 65,536 or an odd byte count is invalid_argument (host checks only)."""
+    from market_sim_b200.head import ErrorCode as E
+
+    f = lib.lib.mf_head_restricted_csr_u16ids_f16_ex
+    rows, hs, total = 4, 576, 10
+    ws = lib.lib.mf_head_workspace_bytes(rows)
+
+    def call(v=1000, ids_bytes=total * 2):
+        s = [rows * hs * 2, v * hs * 2, (rows + 1) * 4, ids_bytes, rows * 4, rows * 4, ws]
+        p = [_p(i) for i in range(7)]
+        args = []
+        for i in range(7):
+            args += [p[i], s[i]]
+        return f(*args, rows, hs, v, 0, ctypes.c_void_p(STREAM)).code
+
+    assert call(v=65537) == E.invalid_argument
+    assert call(ids_bytes=total * 2 + 1) == E.invalid_argument

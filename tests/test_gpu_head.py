@@ -458,6 +458,50 @@ def test_host_pipeline_packed_batches(mf, emb_full):
     pipe.close()
 
 
+def test_u16_ids_equal_int32_ids(mf, emb_full):
+    """The uint16-id layout (``restricted_output_head_csr_u16ids_f16_ex`` and
+    the pipeline's ``submit_packed(..., u16_ids=True)``) gives the int32 path's
+    ids and scores bit for bit, including a row whose candidate is outside the
+    vocabulary (still a u16 value) and an empty row."""
+    import torch
+
+    e, e_dev = emb_full
+    vocab = int(e_dev.shape[0])
+    pipe = mf.HostPipeline(e_dev, 256, 600_000, depth=2)
+    for i, (rows, kmax) in enumerate([(256, 4096), (1, 1), (33, 300)]):
+        h, off, ids = _ragged_case(1300 + i, rows, kmax)
+        if rows == 33:  # row 5: an id past the vocabulary; row 6: empty
+            ids = ids.copy()
+            ids[off[5]] = vocab + 7
+            keep = np.ones(ids.size, bool)
+            keep[off[6]:off[7]] = False
+            n6 = off[7] - off[6]
+            ids = ids[keep]
+            off = off.copy()
+            off[7:] -= n6
+        want, want_sc, _ = _csr_call(mf, h, e_dev, off, ids)
+        out = torch.empty(rows, dtype=torch.int32, device="cuda")
+        sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+        ws = torch.zeros(mf.head_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+        ids16 = torch.from_numpy(ids.astype(np.uint16).view(np.int16)).cuda()
+        st = mf.restricted_output_head_csr_u16ids_f16_ex(to_dev(h), e_dev, to_dev(off), ids16, out,
+                                                         sc, ws, rows, 576, vocab, 0, _stream())
+        assert st.ok(), st
+        torch.cuda.synchronize()
+        assert np.array_equal(_u32(out), want)
+        assert np.array_equal(sc.cpu().numpy().view(np.uint32), want_sc.view(np.uint32))
+        assert int(ws.sum()) == 0  # the workspace is left zero
+        b = mf.HostPipeline.pack(h, off, ids, u16_ids=True)
+        o = torch.empty(2 * rows, dtype=torch.int32).pin_memory()
+        pipe.wait(pipe.submit_packed(b, rows, ids.size, o, u16_ids=True))
+        assert np.array_equal(o.numpy()[:rows].view(np.uint32), want)
+        assert np.array_equal(o.numpy()[rows:].view(np.uint32), want_sc.view(np.uint32))
+    with pytest.raises(RuntimeError, match="invalid_argument"):  # byte count of int32 ids
+        b32 = mf.HostPipeline.pack(h, off, ids)
+        pipe.submit_packed(b32, 33, ids.size, o, u16_ids=True)
+    pipe.close()
+
+
 def test_host_pipeline_wait_on_reused_slot(mf, emb_full):
     """More batches than slots, then wait(ticket 0) alone: the first batch's
     slot has been reused since, and wait must still not return before that
