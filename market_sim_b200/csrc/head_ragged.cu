@@ -469,7 +469,7 @@ __device__ __forceinline__ void stage_row_warp(const RaggedParams& p, uint32_t r
 //     iteration.
 //   * A block spanning more rows (many short rows) stages per group: the
 //     lane's own shared-memory slot by cp.async, normalised in place.
-template <bool kNorm>
+template <bool kNorm, bool kIds16>
 __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
                                                const Rows<RowMode::kCsr>& rows_tab,
                                                int64_t c_begin, int64_t c_end, int sub,
@@ -485,7 +485,7 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
   uint4 e0[kFastChunksPerLane], e1[kFastChunksPerLane];
   auto issue = [&]() {
     has1 = c + 1 < c_end;
-    if (p.ids16) {
+    if constexpr (kIds16) {
       t0 = __ldg(p.ids16 + c);
       t1 = has1 ? __ldg(p.ids16 + c + 1) : 0u;
     } else {
@@ -662,7 +662,7 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
   if (have_row) flush_row<RowMode::kCsr>(p, rows_tab, r, row_b, row_e, best, seen, sub, bs);
 }
 
-template <RowMode M, bool kFast, bool kNorm = false>
+template <RowMode M, bool kFast, bool kNorm = false, bool kIds16 = false>
 __global__ void __launch_bounds__(kThreads, 2)
 ragged_head_kernel(RaggedParams p, int64_t chunk) {
   // Dynamic shared memory: DFA mode, rows + 1 starts then rows arc bases;
@@ -799,7 +799,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
     BlockRowTable tab;
     tab.rows = s_hid + kThreads * kFastChunksPerLane;  // after the per-lane slots
     tab.start = s_tab_start;
-    csr_fast_block<kNorm>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
+    csr_fast_block<kNorm, kIds16>(p, *reinterpret_cast<const Rows<RowMode::kCsr>*>(&rows_tab), c_begin,
                           c_end, sub, gmask, s_hid + threadIdx.x, bs, tab, s_rows_found,
                           s_row_counts);
   } else if (c_begin < c_end) {
@@ -847,7 +847,7 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
         t[j] = 0;
         if constexpr (M == RowMode::kCsr) {
           if (j < n_here)
-            t[j] = p.ids16 ? (uint32_t)__ldg(p.ids16 + c + j) : (uint32_t)__ldg(p.ids + c + j);
+            t[j] = kIds16 ? (uint32_t)__ldg(p.ids16 + c + j) : (uint32_t)__ldg(p.ids + c + j);
         } else if (j < n_here) {
           t[j] = (uint32_t)p.ids[arc_base + c + j];
         }
@@ -1010,6 +1010,8 @@ static DeviceInfo& device_info() {
                          cudaFuncAttributeMaxDynamicSharedMemorySize, kCsrFastSmem);
     cudaFuncSetAttribute(ragged_head_kernel<RowMode::kCsr, true, true>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, kCsrFastSmem);
+    cudaFuncSetAttribute(ragged_head_kernel<RowMode::kCsr, true, false, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, kCsrFastSmem);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
         &d.blocks_per_sm[0][1], ragged_head_kernel<RowMode::kCsr, true>, kThreads, kCsrFastSmem);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
@@ -1106,7 +1108,8 @@ static mf_status csr_head(
       !mul_ok(vocab, hidden_size, &eb) || !mul_ok(eb, 2, &eb) || !mul_ok(rows + 1, 4, &ob))
     return fail(MF_ARITHMETIC_OVERFLOW);
   const uint64_t id_size = ids_u16 ? 2 : 4;
-  if (ids_u16 && vocab > 65536) return fail(MF_INVALID_ARGUMENT);  // ids would not fit 16 bits
+  if (ids_u16 && (vocab > 65536 || gamma))  // ids would not fit 16 bits; no fused-norm variant
+    return fail(MF_INVALID_ARGUMENT);
   if (ids_bytes % id_size != 0 || ids_bytes / id_size > (uint64_t)INT32_MAX)
     return fail(MF_INVALID_ARGUMENT);
   if (hidden_bytes != hb || embedding_bytes != eb || offsets_bytes != ob ||
@@ -1164,7 +1167,12 @@ static mf_status csr_head(
     e = cudaMemsetAsync(workspace, 0, mf_head_workspace_bytes(rows), cfg.stream);
     if (e != cudaSuccess) return fail(MF_CUDA_RUNTIME_FAILURE, (uint32_t)e);
   }
-  if (fast && p.gamma)
+  if (ids_u16)  // (the u16 entry has no fused norm)
+    e = fast ? cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, true, false, true>, p,
+                                  chunk)
+             : cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, false, false, true>, p,
+                                  chunk);
+  else if (fast && p.gamma)
     e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, true, true>, p, chunk);
   else if (fast)
     e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, true>, p, chunk);
