@@ -1142,8 +1142,10 @@ static mf_status csr_head(
   const bool fast = fast_path(hidden, embedding, hidden_size);
   DeviceInfo& d = device_info();
   const int64_t max_blocks = (int64_t)d.sms * d.blocks_per_sm[0][fast ? 1 : 0];
-  // at least 8 candidates per group so tiny batches do not launch idle blocks
-  int64_t blocks = (p.total + (int64_t)kGroupsPerBlock * 8 - 1) / ((int64_t)kGroupsPerBlock * 8);
+  // at least 2 candidates per group so tiny batches do not launch idle blocks
+  // (a floor of 8 made a one-row launch with K = 512 or 4,096 walk 8
+  // dependent iterations per group: 8.5 / 8.8 us against 5.3 / 6.0 us)
+  int64_t blocks = (p.total + (int64_t)kGroupsPerBlock * 2 - 1) / ((int64_t)kGroupsPerBlock * 2);
   blocks = blocks < 1 ? 1 : (blocks > max_blocks ? max_blocks : blocks);
   const int64_t groups = blocks * kGroupsPerBlock;
   int64_t chunk = (p.total + groups - 1) / groups;
