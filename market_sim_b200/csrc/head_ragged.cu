@@ -273,6 +273,29 @@ struct BlockSlots {
   int64_t chunk;            // candidates per group
 };
 
+// CSR batches of up to kLocalCheckRows rows on more than one block: each
+// block's part of a row goes to the row key by one atomicMax that nothing
+// waits on, and a finishing kernel decodes every key after the whole grid (no
+// arrival counter, no finaliser on the critical path of a block).  A
+// one-block grid finalises its rows itself: every row then completes inside
+// the block's shared-memory merge, so no global key is touched and a second
+// launch would only add latency.
+__device__ __forceinline__ bool csr_keys_only(const RaggedParams& p) {
+  return p.rows <= kLocalCheckRows && gridDim.x > 1;
+}
+
+// Malformed offsets found by the per-block check: with the finishing kernel
+// every row key stays zero and decodes to the sentinel; a one-block grid
+// writes the sentinels itself.
+__device__ __forceinline__ void csr_malformed(const RaggedParams& p) {
+  if (csr_keys_only(p)) return;
+  pdl_wait();
+  for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+    p.out_ids[r] = kInvalid;
+    if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+  }
+}
+
 // One flushed (row, key, n) triple: merge and finalise when complete.  A
 // row split between groups first merges in the block's shared slot; only
 // the group that completes the block's part of the row goes on to the
@@ -291,11 +314,7 @@ __device__ void flush_row(const RaggedParams& p, const Rows<M>& rows_tab, uint32
   }
   pdl_wait();  // the workspace and outputs may still belong to the previous launch
   const int64_t row_len = row_e - row_b;
-  // Batches of up to kLocalCheckRows rows: the block's part of the row goes
-  // to the row key by one atomicMax and nothing waits on it; the finishing
-  // kernel decodes every key after the whole grid (no arrival counter, no
-  // finaliser on the critical path of a block).
-  const bool keys_only = M == RowMode::kCsr && p.rows <= kLocalCheckRows;
+  const bool keys_only = M == RowMode::kCsr && csr_keys_only(p);
   if (n == row_len && !keys_only) {  // the group saw the whole row: no merge needed
     finalize_row<M>(p, rows_tab, r, key);
     return;
@@ -516,7 +535,10 @@ __device__ __forceinline__ void csr_fast_block(const RaggedParams& p,
   bool rows_known = false;
   uint32_t known_first = 0, known_last = 0;
   if (p.rows <= kLocalCheckRows) {
-    if (!csr_local_check(p, bs.begin, bs.end, s_row_counts, known_first, known_last)) return;
+    if (!csr_local_check(p, bs.begin, bs.end, s_row_counts, known_first, known_last)) {
+      csr_malformed(p);
+      return;
+    }
     rows_known = true;
   }
   if (!rows_known) {
@@ -695,8 +717,10 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
       uint32_t first, last;  // (only the fast path uses the block's rows)
       if (!csr_local_check(p, min(p.total, (int64_t)blockIdx.x * kGroupsPerBlock * chunk),
                            min(p.total, (int64_t)(blockIdx.x + 1) * kGroupsPerBlock * chunk),
-                           s_row_counts, first, last))
+                           s_row_counts, first, last)) {
+        csr_malformed(p);
         return;
+      }
     }
   } else {
     pdl_trigger();  // the next decode step's blocks may queue behind this one's
@@ -903,9 +927,18 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   if constexpr (M == RowMode::kDfa) return;
   // Offsets checked on entry: the finishing kernel decodes every row key
   // (an empty row's key is zero, which decodes to the sentinel).
-  if (p.rows <= kLocalCheckRows) return;
+  if (csr_keys_only(p)) return;
   // Empty rows get the sentinel here (no group visits them).
   pdl_wait();
+  if (p.rows <= kLocalCheckRows) {  // one block, offsets checked on entry
+    for (uint32_t r = threadIdx.x; r < p.rows; r += kThreads) {
+      if (p.offsets[r] == p.offsets[r + 1]) {
+        p.out_ids[r] = kInvalid;
+        if (p.out_scores) p.out_scores[r] = __uint_as_float(0x7FC00000u);
+      }
+    }
+    return;
+  }
   // Larger batches: decreasing offsets or a bad first/last offset flag the
   // batch for the last block out.
   for (uint32_t r = blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += gridDim.x * kThreads) {
@@ -954,9 +987,9 @@ ragged_head_kernel(RaggedParams p, int64_t chunk) {
   }
 }
 
-// CSR batches of up to kLocalCheckRows rows: after the whole head grid (a
-// programmatic dependent launch that waits for it), every row key to the id
-// and score rows, and the key back to zero for the next call.
+// CSR batches of up to kLocalCheckRows rows on more than one block: after the
+// whole head grid (a programmatic dependent launch that waits for it), every row
+// key to the id and score rows, and the key back to zero for the next call.
 __global__ void csr_finish_kernel(unsigned long long* keys, uint32_t* out_ids, float* out_scores,
                                   uint32_t rows) {
   pdl_trigger();
@@ -1183,7 +1216,7 @@ static mf_status csr_head(
   else
     e = cudaLaunchKernelEx(&cfg, ragged_head_kernel<RowMode::kCsr, false>, p, chunk);
   if (e == cudaSuccess) e = cudaGetLastError();
-  if (e == cudaSuccess && rows <= (uint64_t)kLocalCheckRows) {
+  if (e == cudaSuccess && rows <= (uint64_t)kLocalCheckRows && blocks > 1) {
     cudaLaunchConfig_t fin = {};
     fin.gridDim = dim3((unsigned)((rows + kThreads - 1) / kThreads), 1, 1);
     fin.blockDim = dim3(kThreads, 1, 1);

@@ -299,14 +299,17 @@ def test_csr_ties_nan_and_mixed(mf, O):
     assert got[4] == oid[4]
 
 
-def test_csr_malformed_offsets_gives_sentinel_and_recovers(mf, O, emb_full):
+@pytest.mark.parametrize("rows,kmax", [(16, 256), (3, 16)])
+def test_csr_malformed_offsets_gives_sentinel_and_recovers(mf, O, emb_full, rows, kmax):
+    """(16, 256): a grid of several blocks, rows decoded by the finishing
+    kernel; (3, 16): a one-block grid that finalises its rows itself."""
     import torch
 
     e, e_dev = emb_full
-    h, off, ids = _ragged_case(4, 16, 256)
+    h, off, ids = _ragged_case(4, rows, kmax)
     bad = off.copy()
-    bad[5], bad[6] = bad[6], bad[5]  # decreasing step
-    ws = torch.zeros(mf.head_workspace_bytes(16), dtype=torch.uint8, device="cuda")
+    bad[1] = bad[2] + 1  # decreasing step
+    ws = torch.zeros(mf.head_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
     got, sc, ws = _csr_call(mf, h, e_dev, bad, ids, ws=ws)
     assert (got == INVALID).all() and np.isnan(sc).all()
     assert int(ws.sum()) == 0
