@@ -102,9 +102,10 @@ MF_API mf_status mf_restricted_output_head_f16(const void* hidden, uint64_t hidd
  * the whole batch are split evenly over the GPU, so one long row is shared
  * by many thread blocks; partial results merge through 64-bit atomic max on
  * a packed (score, id) key in `workspace`, which makes the result
- * independent of scheduling.  A call is two kernels on `stream`: the head,
- * and (batches of up to 4,096 rows) a small kernel that decodes the row keys
- * into out_ids / out_scores and clears them.
+ * independent of scheduling.  A call is the head kernel on `stream`, and, for
+ * batches of up to 4,096 rows that span more than one thread block, a small
+ * second kernel that decodes the row keys into out_ids / out_scores and
+ * clears them.
  *
  * workspace: mf_head_workspace_bytes(rows) bytes of device memory, zero-filled
  * once by the caller before its first use; every call leaves it zero again.
