@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <initializer_list>
+#include <utility>
 
 #include "common.cuh"
 
@@ -215,6 +216,13 @@ bool distinct(std::initializer_list<const void*> ptrs) {
   }
   return true;
 }
+// Every buffer starts on a multiple of the widest element the kernels
+// access in it: a misaligned pointer is invalid_argument, not a device fault.
+bool aligned(std::initializer_list<std::pair<const void*, uintptr_t>> bufs) {
+  for (const auto& b : bufs)
+    if ((uintptr_t)b.first % b.second != 0) return false;
+  return true;
+}
 
 }  // namespace
 
@@ -231,7 +239,8 @@ extern "C" mf_status mf_greedy_select_f16(const void* logits, uint64_t logits_by
   uint64_t elems, lb, tb;
   if (!mul_ok(rows, vocab, &elems) || !mul_ok(elems, 2, &lb) || !mul_ok(rows, 4, &tb))
     return fail(MF_ARITHMETIC_OVERFLOW);
-  if (logits_bytes != lb || token_ids_bytes != tb || !distinct({logits, token_ids}))
+  if (logits_bytes != lb || token_ids_bytes != tb || !distinct({logits, token_ids}) ||
+      !aligned({{logits, 2}, {token_ids, 4}}))
     return fail(MF_INVALID_ARGUMENT);
   const bool vec = vocab % 8 == 0 && (uintptr_t)logits % 16 == 0;
   greedy_kernel<<<(unsigned)rows, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -253,7 +262,8 @@ extern "C" mf_status mf_restricted_greedy_select_f16(
       !mul_ok(ae, 4, &ab) || !mul_ok(rows, 4, &rb))
     return fail(MF_ARITHMETIC_OVERFLOW);
   if (logits_bytes != lb || allowed_bytes != ab || counts_bytes != rb || token_ids_bytes != rb ||
-      !distinct({logits, allowed, counts, token_ids}))
+      !distinct({logits, allowed, counts, token_ids}) ||
+      !aligned({{logits, 2}, {allowed, 4}, {counts, 4}, {token_ids, 4}}))
     return fail(MF_INVALID_ARGUMENT);
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   restricted_select_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -279,7 +289,8 @@ extern "C" mf_status mf_restricted_output_head_f16(
       !mul_ok(ae, 4, &ab) || !mul_ok(rows, 4, &rb))
     return fail(MF_ARITHMETIC_OVERFLOW);
   if (hidden_bytes != hb || embedding_bytes != eb || allowed_bytes != ab || counts_bytes != rb ||
-      token_ids_bytes != rb || !distinct({hidden, embedding, allowed, counts, token_ids}))
+      token_ids_bytes != rb || !distinct({hidden, embedding, allowed, counts, token_ids}) ||
+      !aligned({{hidden, 2}, {embedding, 2}, {allowed, 4}, {counts, 4}, {token_ids, 4}}))
     return fail(MF_INVALID_ARGUMENT);
   if (hidden_size > UINT32_MAX) return fail(MF_RESOURCE_LIMIT);
   const bool fast = hidden_size == (uint64_t)kFastHidden && (uintptr_t)hidden % 16 == 0 &&

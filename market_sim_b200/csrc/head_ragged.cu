@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <initializer_list>
+#include <utility>
 #include <mutex>
 
 #include "common.cuh"
@@ -1091,6 +1092,16 @@ bool distinct(std::initializer_list<const void*> ptrs) {
   return true;
 }
 
+// Every buffer starts on a multiple of the widest element the kernels load
+// from or store to it (2-byte halves, 4-byte ints, 8-byte keys); a
+// misaligned pointer is invalid_argument, not a device fault.  Null passes
+// (the callers check which buffers may be null).
+bool aligned(std::initializer_list<std::pair<const void*, uintptr_t>> bufs) {
+  for (const auto& b : bufs)
+    if ((uintptr_t)b.first % b.second != 0) return false;
+  return true;
+}
+
 bool fast_path(const void* hidden, const void* embedding, uint64_t hidden_size) {
   return hidden_size == (uint64_t)kFastHidden && ((uintptr_t)hidden % 16) == 0 &&
          ((uintptr_t)embedding % 16) == 0;
@@ -1152,6 +1163,9 @@ static mf_status csr_head(
   if (!distinct({hidden, embedding, offsets, out_ids, workspace}) ||
       (ids_bytes && !distinct({ids, hidden, embedding, offsets, out_ids, workspace})) ||
       (out_scores && !distinct({out_scores, hidden, embedding, offsets, out_ids, workspace})))
+    return fail(MF_INVALID_ARGUMENT);
+  if (!aligned({{hidden, 2}, {embedding, 2}, {offsets, 4}, {ids, id_size}, {out_ids, 4},
+                {out_scores, 4}, {workspace, 8}, {gamma, 2}}))
     return fail(MF_INVALID_ARGUMENT);
 
   RaggedParams p{};
@@ -1306,7 +1320,8 @@ mf_status dfa_validate(const void* hidden, uint64_t hidden_bytes, const void* em
       arc_tokens_bytes == 0 || arc_tokens_bytes % 4 != 0 || arc_next_bytes != arc_tokens_bytes ||
       arc_tokens_bytes / 4 > (uint64_t)INT32_MAX)
     return fail(MF_INVALID_ARGUMENT);
-  if (!distinct({hidden, embedding, state_offsets, arc_tokens, arc_next}))
+  if (!distinct({hidden, embedding, state_offsets, arc_tokens, arc_next}) ||
+      !aligned({{hidden, 2}, {embedding, 2}, {state_offsets, 4}, {arc_tokens, 4}, {arc_next, 4}}))
     return fail(MF_INVALID_ARGUMENT);
   return ok();
 }
@@ -1358,7 +1373,9 @@ static mf_status dfa_step(
       out_tokens_bytes != batch * 4 || (out_scores && out_scores_bytes != batch * 4) ||
       workspace_bytes < mf_head_workspace_bytes(batch) ||  // one step: no key buffers
       !distinct({states_in, states_out, out_tokens, workspace, hidden, embedding}) ||
-      (out_scores && !distinct({out_scores, states_in, states_out, out_tokens, workspace})))
+      (out_scores && !distinct({out_scores, states_in, states_out, out_tokens, workspace})) ||
+      !aligned({{states_in, 4}, {states_out, 4}, {out_tokens, 4}, {out_scores, 4},
+                {workspace, 8}, {gamma, 2}}))
     return fail(MF_INVALID_ARGUMENT);
   RaggedParams p{};
   p.hidden = static_cast<const __half*>(hidden);
@@ -1436,7 +1453,8 @@ extern "C" mf_status mf_dfa_decode_f16(
   if (state_trace_bytes != tb + batch * 4 || token_trace_bytes != tb ||
       (score_trace && score_trace_bytes != tb) || workspace_bytes < mf_dfa_workspace_bytes(batch) ||
       !distinct({state_trace, token_trace, workspace, hidden, embedding}) ||
-      (score_trace && !distinct({score_trace, state_trace, token_trace, workspace})))
+      (score_trace && !distinct({score_trace, state_trace, token_trace, workspace})) ||
+      !aligned({{state_trace, 4}, {token_trace, 4}, {score_trace, 4}, {workspace, 8}}))
     return fail(MF_INVALID_ARGUMENT);
   const bool fast = fast_path(hidden, embedding, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

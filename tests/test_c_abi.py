@@ -204,3 +204,46 @@ def test_csr_u16ids_rejections(lib):
 
     assert call(v=65537) == E.invalid_argument
     assert call(ids_bytes=total * 2 + 1) == E.invalid_argument
+
+
+def test_misaligned_buffers_rejected(lib):
+    """A buffer that does not start on a multiple of its widest element (2-byte
+    halves, 4-byte ints, 8-byte workspace keys) is invalid_argument on the
+    host, never a device fault (checked before any CUDA call)."""
+    from market_sim_b200.head import ErrorCode as E
+
+    rows, hs, v, total = 4, 576, 1000, 10
+    ws = lib.lib.mf_head_workspace_bytes(rows)
+
+    def csr(bump):
+        f = lib.lib.mf_head_restricted_csr_f16
+        s = [rows * hs * 2, v * hs * 2, (rows + 1) * 4, total * 4, rows * 4, rows * 4, ws]
+        p = [ctypes.c_void_p(FAKE[i] + bump.get(i, 0)) for i in range(7)]
+        args = []
+        for i in range(7):
+            args += [p[i], s[i]]
+        return f(*args, rows, hs, v, ctypes.c_void_p(STREAM)).code
+
+    assert csr({2: 2}) == E.invalid_argument  # offsets
+    assert csr({3: 2}) == E.invalid_argument  # int32 ids
+    assert csr({4: 2}) == E.invalid_argument  # out ids
+    assert csr({6: 4}) == E.invalid_argument  # workspace (8-byte keys)
+    assert csr({0: 1}) == E.invalid_argument  # hidden halves
+
+    f = lib.lib.mf_restricted_output_head_f16
+    r, mx = 1, 2
+    sz = [r * hs * 2, v * hs * 2, r * mx * 4, r * 4, r * 4]
+    p = [ctypes.c_void_p(FAKE[i] + (2 if i == 2 else 0)) for i in range(5)]
+    assert f(p[0], sz[0], p[1], sz[1], p[2], sz[2], p[3], sz[3], p[4], sz[4], r, hs, v, mx,
+             ctypes.c_void_p(STREAM)).code == E.invalid_argument  # allowed ids
+
+    f = lib.lib.mf_dfa_decode_f16
+    steps, batch, ns, arcs = 3, 4, 5, 9
+    dws = lib.lib.mf_dfa_workspace_bytes(batch)
+    s = [steps * batch * hs * 2, v * hs * 2, (ns + 1) * 4, arcs * 4, arcs * 4,
+         (steps + 1) * batch * 4, steps * batch * 4, steps * batch * 4, dws]
+    p = [ctypes.c_void_p(FAKE[i] + (2 if i == 3 else 0)) for i in range(9)]
+    args = []
+    for i in range(9):
+        args += [p[i], s[i]]
+    assert f(*args, steps, batch, ns, hs, v, ctypes.c_void_p(STREAM)).code == E.invalid_argument
