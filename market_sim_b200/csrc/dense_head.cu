@@ -693,7 +693,9 @@ mf_status dense_launch(const void* hidden, uint64_t hidden_bytes, const void* em
       embedding == nullptr || workspace == nullptr ||
       (out_keys == nullptr && out_ids == nullptr) ||
       !d_distinct({hidden, embedding, out_keys, out_ids, out_scores, workspace}) ||
-      (uintptr_t)hidden % 16 != 0 || (uintptr_t)embedding % 16 != 0)
+      (uintptr_t)hidden % 16 != 0 || (uintptr_t)embedding % 16 != 0 ||
+      (uintptr_t)out_keys % 8 != 0 || (uintptr_t)out_ids % 4 != 0 ||
+      (uintptr_t)out_scores % 4 != 0 || (uintptr_t)workspace % 8 != 0)
     return d_fail(MF_INVALID_ARGUMENT);
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -854,7 +856,8 @@ extern "C" mf_status mf_decode_keys(const void* keys, uint64_t keys_bytes, void*
     return d_fail(MF_INVALID_ARGUMENT);
   if (rows > (uint64_t)INT32_MAX) return d_fail(MF_RESOURCE_LIMIT);
   if (keys_bytes != rows * 8 || out_ids_bytes != rows * 4 ||
-      (out_scores && out_scores_bytes != rows * 4) || !d_distinct({keys, out_ids, out_scores}))
+      (out_scores && out_scores_bytes != rows * 4) || !d_distinct({keys, out_ids, out_scores}) ||
+      (uintptr_t)keys % 8 != 0 || (uintptr_t)out_ids % 4 != 0 || (uintptr_t)out_scores % 4 != 0)
     return d_fail(MF_INVALID_ARGUMENT);
   decode_keys_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const unsigned long long*>(keys), (uint32_t)rows, static_cast<uint32_t*>(out_ids),

@@ -247,3 +247,22 @@ def test_misaligned_buffers_rejected(lib):
     for i in range(9):
         args += [p[i], s[i]]
     assert f(*args, steps, batch, ns, hs, v, ctypes.c_void_p(STREAM)).code == E.invalid_argument
+
+
+def test_dense_misaligned_outputs_rejected(lib):
+    """The dense head and mf_decode_keys reject output buffers that are not
+    aligned to their element size (host check, before any CUDA call)."""
+    from market_sim_b200.head import ErrorCode as E
+
+    rows, hs, v = 4, 576, 1024
+    f = lib.lib.mf_dense_head_f16
+    ws = lib.lib.mf_dense_workspace_bytes(rows)
+    s = [rows * hs * 2, v * hs * 2, rows * 8, rows * 4, rows * 4, ws]
+    p = [ctypes.c_void_p(FAKE[i] + (2 if i == 3 else 0)) for i in range(6)]
+    args = []
+    for i in range(6):
+        args += [p[i], s[i]]
+    assert f(*args, rows, hs, v, 0, ctypes.c_void_p(STREAM)).code == E.invalid_argument
+    g = lib.lib.mf_decode_keys
+    assert g(ctypes.c_void_p(FAKE[0] + 4), rows * 8, _p(1), rows * 4, None, 0, rows,
+             ctypes.c_void_p(STREAM)).code == E.invalid_argument
