@@ -13,6 +13,9 @@
  *   a size product overflowing uint64             -> MF_ARITHMETIC_OVERFLOW
  *   a byte size that does not match exactly, a null or aliased buffer
  *                                                 -> MF_INVALID_ARGUMENT
+ *   a buffer not aligned to its widest element (2-byte halves, 4-byte
+ *   ints and scores, 8-byte keys and workspace; cudaMalloc memory always
+ *   is)                                           -> MF_INVALID_ARGUMENT
  *   the launch failing                            -> MF_CUDA_BACKEND_FAILURE,
  *                                                    detail = cudaError_t
  * Bad rows found on the device produce MF_INVALID_TOKEN, never a trap.
