@@ -322,6 +322,34 @@ def test_csr_malformed_offsets_gives_sentinel_and_recovers(mf, O, emb_full, rows
     check_head_parity(got, sc, oid, obest, oru)
 
 
+def test_csr_large_batch_counter_path(mf, O, emb_full):
+    """Batches above 4,096 rows take the other merge path (per-row arrival
+    counters, in-kernel finaliser, a grid-wide offsets check by the last block
+    out): parity with the oracle, an empty row, malformed offsets giving every
+    row the sentinel with the workspace left zero, and a good call after it."""
+    e, e_dev = emb_full
+    rows = 5000
+    h, off, ids = _ragged_case(21, rows, 8)
+    off = off.copy()
+    n7 = off[8] - off[7]  # row 7 empty
+    keep = np.ones(ids.size, bool)
+    keep[off[7]:off[8]] = False
+    ids = ids[keep]
+    off[8:] -= n7
+    got, sc, ws = _csr_call(mf, h, e_dev, off, ids)
+    oid, obest, oru = O.restricted_head_csr(h, e, off, ids)
+    check_head_parity(got, sc, oid, obest, oru)
+    assert got[7] == INVALID
+    assert int(ws.sum()) == 0
+    bad = off.copy()
+    bad[100] = bad[101] + 1  # decreasing step
+    got, sc, ws = _csr_call(mf, h, e_dev, bad, ids, ws=ws)
+    assert (got == INVALID).all() and np.isnan(sc).all()
+    assert int(ws.sum()) == 0
+    got, sc, ws = _csr_call(mf, h, e_dev, off, ids, ws=ws)
+    check_head_parity(got, sc, oid, obest, oru)
+
+
 def test_csr_deterministic_repeats(mf, emb_full):
     _, e_dev = emb_full
     h, off, ids = _ragged_case(9, 128, 4096)
