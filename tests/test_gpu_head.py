@@ -533,6 +533,38 @@ def test_u16_ids_equal_int32_ids(mf, emb_full):
     pipe.close()
 
 
+def test_u16_ids_generic_width(mf):
+    """The uint16-id entry on the generic (any hidden width) kernel equals the
+    int32 entry bit for bit: 9 rows of width 40 over a 300-row table."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    rows, width, vocab = 9, 40, 300
+    h = torch.from_numpy(rng.standard_normal((rows, width)).astype(np.float16)).cuda()
+    emb = torch.from_numpy((0.1 * rng.standard_normal((vocab, width))).astype(np.float16)).cuda()
+    counts = rng.integers(0, 30, rows)
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    ids = rng.integers(0, vocab, int(off[-1])).astype(np.int32)
+    outs = []
+    for u16 in (False, True):
+        out = torch.empty(rows, dtype=torch.int32, device="cuda")
+        sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+        ws = torch.zeros(mf.head_workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+        if u16:
+            d = torch.from_numpy(ids.astype(np.uint16).view(np.int16)).cuda()
+            st = mf.restricted_output_head_csr_u16ids_f16_ex(h, emb, to_dev(off), d, out, sc, ws,
+                                                             rows, width, vocab, 0, _stream())
+        else:
+            st = mf.restricted_output_head_csr_f16_ex(h, emb, to_dev(off), to_dev(ids), out, sc, ws,
+                                                      rows, width, vocab, 0, _stream())
+        assert st.ok(), st
+        torch.cuda.synchronize()
+        outs.append((_u32(out), sc.cpu().numpy().view(np.uint32)))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+    assert (outs[0][0][counts == 0] == INVALID).all()
+
+
 def test_host_pipeline_wait_on_reused_slot(mf, emb_full):
     """More batches than slots, then wait(ticket 0) alone: the first batch's
     slot has been reused since, and wait must still not return before that
